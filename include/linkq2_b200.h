@@ -1,0 +1,151 @@
+/*
+ * linkq2_b200 — C ABI of the B200 (sm_100a) W4A16 and KV4 operators.
+ *
+ * Every entry point takes raw device pointers, sizes, element strides and a
+ * CUDA stream (a cudaStream_t passed as void*), enqueues its kernels on that
+ * stream and returns at once.  Nothing here allocates, frees or synchronises;
+ * no entry point keeps state between calls.  The return value is LQ2_OK or an
+ * LQ2_ERR_* code describing which argument was rejected; a rejected call
+ * launches nothing.
+ *
+ * Paths cited below are relative to the LinkQ2 project root and name the
+ * reference interface each function stands in for.
+ */
+#ifndef LINKQ2_B200_H
+#define LINKQ2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LQ2_OK 0
+#define LQ2_ERR_ARG 1        /* null pointer or non-positive size */
+#define LQ2_ERR_SHAPE 2      /* shape the operator does not support */
+#define LQ2_ERR_ALIGN 3      /* pointer or stride misaligned for vector access */
+#define LQ2_ERR_WORKSPACE 4  /* workspace missing or smaller than *_workspace_bytes */
+#define LQ2_ERR_CUDA 5       /* the launch itself was refused by the CUDA runtime */
+
+/* Human-readable text for a status code. */
+const char* lq2_status_string(int status);
+
+/* ABI revision; bumped whenever a signature below changes. */
+int lq2_abi_version(void);
+
+/* --------------------------------------------------------------------------
+ * W4A16 linear
+ * -------------------------------------------------------------------------- */
+
+/*
+ * Load-time packing, replacing pack_weights_over_cols_triton(codes, 4, 32,
+ * transpose=True).contiguous() and the "+8" of symmetric checkpoints
+ * (qslab/kernels/gemlite/bitpack.py:96-125, qslab/runtime/backends/gemlite.py:22-25).
+ *
+ *   values  [N, K] int8   logical checkpoint integers (-8..7 symmetric, 0..15 affine)
+ *   offset  8 for symmetric checkpoints, 0 for affine ones
+ *   packed  [K/8, N] int32, n fastest: word(k8, n) = sum_j (values[n, 8*k8+j] + offset) << 4j
+ * K must be a multiple of 8.
+ */
+int lq2_w4_pack(const int8_t* values, int offset, int32_t* packed, int n, int k, void* stream);
+
+/*
+ * Bytes of scratch lq2_w4a16_linear needs for this problem size (0 is possible).
+ * The buffer must be zero-filled once when it is created; each call leaves it
+ * zero-filled again where it needs zeros, so it can be reused by later calls on
+ * the same stream.  Two calls that may overlap on the GPU need two buffers.
+ */
+size_t lq2_w4a16_workspace_bytes(int m, int n, int k);
+
+/*
+ * y[M, N] = x[M, K] . dequant(W)^T, replacing qslab.kernels.gemlite.ops.linear
+ * and its three Triton routes (qslab/kernels/gemlite/ops.py:10-15;
+ * triton_kernels/gemv_revsplitK_A16fWnO16f_int32packing.py:155-384,
+ * gemm_splitK_A16fWnO16f_int32packing.py:199-412, gemm_A16fWnO16f_int32packing.py:174-373)
+ * with W_group_mode 3 dequantisation (u - z) * s (triton_kernels/utils.py:66-71).
+ *
+ *   x          [M, K] fp16, row stride x_row_stride elements, unit inner stride
+ *   packed     [K/8, N] int32 (layout of lq2_w4_pack)
+ *   scales     [K/group, N] fp16
+ *   zeros      [K/group, N] fp16 per-group zero points, or NULL for the
+ *              symmetric scalar zero 8
+ *   y          [M, N] fp16 contiguous
+ *   group      power of two >= 32 dividing K;  N a multiple of 32
+ *   workspace  lq2_w4a16_workspace_bytes(M, N, K) bytes (see above)
+ * Products are accumulated in fp32 and rounded to fp16 once.
+ */
+int lq2_w4a16_linear(const void* x, int64_t x_row_stride, const int32_t* packed,
+                     const void* scales, const void* zeros, void* y, int m, int n, int k,
+                     int group, void* workspace, size_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------------------------
+ * KV4 cache.  Pool layout (qslab/runtime/execute/model_runner.py:146-156):
+ *   kq, vq  [S, HKV, D/8] 32-bit words, 8 offset-binary nibbles per word
+ *   ks      [HKV, D] fp16 static per-channel K scale
+ *   vs      [S, HKV, D/v_group] fp16 per-token per-group V scale
+ * -------------------------------------------------------------------------- */
+
+/*
+ * Quantize and scatter one batch of tokens, replacing store_kv_quant
+ * (qslab/kernels/kv4/store.py:9-68).  slot -1 skips the token; any other slot
+ * outside [0, num_slots) is skipped as well instead of being written.
+ *
+ *   k, v       [T, HKV, D] fp16; token stride k_stride / v_stride elements,
+ *              head stride D, unit inner stride (slices of a fused QKV buffer work)
+ *   slots      [T] int32
+ * D a multiple of 8, v_group a multiple of 8 dividing D.
+ */
+int lq2_kv4_store(const void* k, const void* v, int64_t k_stride, int64_t v_stride,
+                  uint32_t* kq, const void* ks, uint32_t* vq, void* vs, const int32_t* slots,
+                  int tokens, int hkv, int d, int v_group, int64_t num_slots, void* stream);
+
+/*
+ * Number of KV splits lq2_kv4_attention will use.  It depends on shapes only
+ * (never on device values), so a captured CUDA graph stays valid
+ * (same property as qslab/kernels/kv4/paged_attention.py:127-131).
+ */
+int lq2_kv4_attention_splits(int batch, int verify_m, int hq, int hkv, int d, int page,
+                             int max_blocks);
+
+/* Scratch bytes for lq2_kv4_attention; same zero-fill contract as the W4A16 workspace. */
+size_t lq2_kv4_attention_workspace_bytes(int batch, int verify_m, int hq, int hkv, int d,
+                                         int page, int max_blocks);
+
+/*
+ * Paged attention over the int4 pool for one query position per sequence
+ * (verify_m == 1) or verify_m consecutive positions, replacing
+ * paged_attention_decode and its kernels
+ * (qslab/kernels/kv4/paged_attention.py:11-150, grouped_attention.py:7-63).
+ *
+ *   q             [batch*verify_m, HQ, D] fp16, row stride q_row_stride elements
+ *   block_tables  [batch, max_blocks] int32, negative entries are padding
+ *   context_lens  [batch] int32; row seq*verify_m + m attends to logical
+ *                 positions [0, context_lens[seq] + m) capped at max_blocks*page
+ *   out           [batch*verify_m, HQ, D] fp16 contiguous
+ * Positions under a negative block-table entry are masked; a row without any
+ * valid position yields zeros.  Block ids are clamped into the pool
+ * ([0, num_slots/page)) before any address is formed.
+ * D must be 64 or 128, HQ a multiple of HKV with verify_m*HQ/HKV <= 64,
+ * page a multiple of 16.
+ */
+int lq2_kv4_attention(const void* q, int64_t q_row_stride, const uint32_t* kq, const void* ks,
+                      const uint32_t* vq, const void* vs, const int32_t* block_tables,
+                      const int32_t* context_lens, void* out, int batch, int verify_m, int hq,
+                      int hkv, int d, int page, int max_blocks, int v_group, int64_t num_slots,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Prefix restore: gather the given slots and dequantise them to fp16
+ * [T, HKV, D], replacing materialize_kv (qslab/kernels/kv4/layout.py:9-47).
+ * Order of slots is kept and duplicates are allowed.  Each value is
+ * fp16(fp32(nibble - 8) * fp32(scale)).  Slots outside [0, num_slots) produce zeros.
+ */
+int lq2_kv4_materialize(const uint32_t* kq, const void* ks, const uint32_t* vq, const void* vs,
+                        const int64_t* slots, void* k_out, void* v_out, int tokens, int hkv,
+                        int d, int v_group, int64_t num_slots, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LINKQ2_B200_H */

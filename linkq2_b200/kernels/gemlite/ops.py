@@ -1,0 +1,50 @@
+"""``linear(x, packed, scales, zeros, meta)`` — the launch interface of the
+reference's W4A16 kernels (``qslab/kernels/gemlite/ops.py:10-15``) backed by the
+sm_100a kernels of this package."""
+from __future__ import annotations
+
+import torch
+
+from linkq2_b200 import _lib, _workspace
+
+
+def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+           meta) -> torch.Tensor:
+    """``x [..., K] fp16`` times the dequantised ``[K, N]`` weight -> ``[..., N] fp16``.
+
+    ``packed [K/8, N] int32``, ``scales [K/G, N] fp16``; ``zeros`` is either the
+    ``[K/G, N] fp16`` zero-point table or a one-element tensor, which selects
+    the symmetric scalar zero 8 exactly as ``zeros.numel() == 1`` does in the
+    reference (``triton_kernels/gemv_revsplitK_A16fWnO16f_int32packing.py:376``).
+    ``meta`` is the 12-tuple built by ``from_quantized``; only its bit width,
+    group size and group mode are read.
+    """
+    if meta[0] != 4 or meta[9] != 3:
+        raise ValueError("only 4-bit weights with (u - zero) * scale dequantisation are supported")
+    group = int(meta[1])
+    if x.dtype != torch.float16:
+        raise TypeError(f"the B200 W4A16 kernels compute in fp16, got {x.dtype}")
+    if not x.is_cuda:
+        raise RuntimeError("linkq2_b200 operators run on CUDA tensors only")
+    k8, n = packed.shape
+    k = k8 * 8
+    if x.shape[-1] != k:
+        raise ValueError(f"expected input width {k}, got {x.shape[-1]}")
+    shape = x.shape[:-1] + (n,)
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    y = torch.empty((m, n), dtype=torch.float16, device=x.device)
+    if m == 0:
+        return y.view(shape)
+    zero_ptr = None if zeros.numel() == 1 else zeros.data_ptr()
+    with torch.cuda.device(x.device):
+        need = _lib.lib.lq2_w4a16_workspace_bytes(m, n, k)
+        ws = _workspace.get("w4a16", need, x.device)
+        stream = torch.cuda.current_stream().cuda_stream
+        status = _lib.lib.lq2_w4a16_linear(
+            x2.data_ptr(), x2.stride(0), packed.data_ptr(), scales.data_ptr(), zero_ptr, y.data_ptr(),
+            m, n, k, group, ws.data_ptr(), ws.numel(), stream)
+    _lib.check(status, "lq2_w4a16_linear")
+    return y.view(shape)

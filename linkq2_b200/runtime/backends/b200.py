@@ -1,0 +1,54 @@
+"""W4A16 Linear backed by the sm_100a kernels of this package.
+
+Drop-in for ``GemLiteLinear`` (``qslab/runtime/backends/gemlite.py:8-43``): same
+constructor contract, same buffer names, shapes and dtypes (``packed [K/8, N]
+int32``, ``scales [K/G, N] fp16``, ``zeros`` 0-dim int32 8 or ``[K/G, N] fp16``,
+``input_scale [K]`` or ``None``), same exceptions."""
+import torch
+
+from linkq2_b200.kernels.gemlite.bitpack import pack_w4
+from linkq2_b200.kernels.gemlite.ops import linear
+from linkq2_b200.runtime.backends.base import QuantLinear
+
+# The metadata tuple the reference hands to its kernels (gemlite.py:33-34):
+# W_nbits, group_size, unpack_mask, elements_per_sample, input dtype, output
+# dtype, accumulator dtype, meta dtype, channel_scale_mode, W_group_mode,
+# data_contiguous, type_id.  Dtype codes follow kernels/gemlite/dtypes.py:5-8.
+_FP32, _FP16 = 0, 1
+
+
+class B200Linear(QuantLinear):
+    @classmethod
+    @torch.no_grad()
+    def from_quantized(cls, values, scale, *, group_size, symmetric,
+                       zero_point=None, input_scale=None, device, dtype):
+        if dtype not in (torch.float16, torch.bfloat16):
+            raise TypeError("W4A16 requires FP16 or BF16 activations")
+        if dtype != torch.float16:
+            raise TypeError("the B200 W4A16 kernels compute in FP16; BF16 activations are not supported")
+        n, k = values.shape
+        if group_size < 32 or group_size & (group_size - 1) or k % group_size or n % 32:
+            raise ValueError(f"unsupported W4A16 shape/group: N={n}, K={k}, group={group_size}")
+        if not symmetric and zero_point is None:
+            raise ValueError("affine checkpoints need a zero_point tensor")
+        layer = cls()
+        layer.in_features, layer.out_features = k, n
+        layer.group_size, layer.compute_dtype = group_size, dtype
+        codes = values.to(device=device)
+        codes = codes.to(torch.int8) if codes.dtype not in (torch.int8, torch.uint8) else codes
+        layer.register_buffer("packed", pack_w4(codes, symmetric))
+        layer.register_buffer("scales", scale.to(device=device, dtype=torch.float16).t().contiguous())
+        zeros = (torch.tensor(8, dtype=torch.int32, device=device) if symmetric
+                 else zero_point.to(device=device, dtype=torch.float16).t().contiguous())
+        layer.register_buffer("zeros", zeros)
+        layer.register_buffer("input_scale", None if input_scale is None
+                              else input_scale.to(device=device, dtype=dtype))
+        layer._meta = (4, group_size, 15, 8, _FP16, _FP16, _FP32, _FP16, 0, 3, True, 104)
+        return layer
+
+    def forward(self, x):
+        if x.dtype != self.compute_dtype:
+            raise TypeError(f"expected {self.compute_dtype}, got {x.dtype}")
+        if self.input_scale is not None:
+            x = x / self.input_scale
+        return linear(x, self.packed, self.scales, self.zeros, self._meta)

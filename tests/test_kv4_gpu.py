@@ -1,0 +1,212 @@
+"""KV4 kernels on the GPU against the golden fixtures and the CPU oracle.
+
+Pool bytes (codes and V scales) and the prefix restore are compared bit for
+bit.  Attention outputs use the reference's own tolerance, max |delta| < 2e-3
+(``tests/kernels/test_kv4_verify.py:116``, ``test_kv4_materialize.py:73``)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import kv4 as ok
+
+pytestmark = pytest.mark.gpu
+
+STORE_CASES = ["static_g64", "static_g32_strided", "static_g128", "static_d64"]
+ATTN_CASES = ["decode_small", "decode_split", "verify_small", "verify_m16", "verify_neg1", "decode_g32"]
+ATOL = 2e-3
+
+
+def t(a):
+    return torch.from_numpy(np.ascontiguousarray(a))
+
+
+def cuda_pool(kc, vc, word_dtype=torch.int32):
+    (kq, ks), (vq, vs) = kc, vc
+    kq, vq = kq.cuda(), vq.cuda()
+    if word_dtype == torch.uint32:
+        kq, vq = kq.view(torch.uint32), vq.view(torch.uint32)
+    return (kq, ks.cuda()), (vq, vs.cuda())
+
+
+def words(x):
+    x = x.cpu()
+    return x.view(torch.int32) if x.dtype == torch.uint32 else x
+
+
+@pytest.mark.parametrize("name", STORE_CASES)
+@pytest.mark.parametrize("word_dtype", [torch.int32, torch.uint32])
+def test_golden_store_and_materialize_bit_exact(golden, name, word_dtype):
+    from linkq2_b200.kernels.kv4 import materialize_kv, store_kv_quant
+    g = golden("kv4_store")
+    tokens, h, d, group, _, strided, slots_total = (int(v) for v in g[f"{name}.meta"])
+    k, v = t(g[f"{name}.k"]).cuda(), t(g[f"{name}.v"]).cuda()
+    if strided:
+        fused = torch.zeros(tokens, h * 3, d, dtype=torch.float16, device="cuda")
+        fused[:, h:2 * h], fused[:, 2 * h:] = k, v
+        _, k, v = fused.chunk(3, dim=1)
+        assert not k.is_contiguous()
+    kc, vc = ok.empty_pool(slots_total, h, d, group)
+    kc[1].copy_(t(g[f"{name}.ks"]))
+    kc, vc = cuda_pool(kc, vc, word_dtype)
+    store_kv_quant(k, v, kc, vc, t(g[f"{name}.slots"]).cuda(), v_group=group)
+    assert torch.equal(words(kc[0]), t(g[f"{name}.kq"]))
+    assert torch.equal(words(vc[0]), t(g[f"{name}.vq"]))
+    assert torch.equal(vc[1].cpu(), t(g[f"{name}.vs"]))
+    km, vm = materialize_kv(kc, vc, t(g[f"{name}.sel"]).cuda(), v_group=group)
+    assert torch.equal(km.cpu(), t(g[f"{name}.km"]))
+    assert torch.equal(vm.cpu(), t(g[f"{name}.vm"]))
+
+
+def test_golden_store_ties_and_saturation(golden):
+    from linkq2_b200.kernels.kv4 import store_kv_quant
+    g = golden("kv4_store")
+    kc = (torch.zeros(4, 1, 8, dtype=torch.int32, device="cuda"), t(g["ties.ks"]).cuda())
+    vc = (torch.zeros(4, 1, 8, dtype=torch.int32, device="cuda"),
+          torch.zeros(4, 1, 1, dtype=torch.float16, device="cuda"))
+    store_kv_quant(t(g["ties.k"]).cuda(), t(g["ties.v"]).cuda(), kc, vc,
+                   torch.tensor([2], dtype=torch.int32, device="cuda"), v_group=64)
+    assert torch.equal(kc[0].cpu(), t(g["ties.kq"]))
+    assert torch.equal(vc[0].cpu(), t(g["ties.vq"]))
+    assert torch.equal(vc[1].cpu(), t(g["ties.vs"]))
+
+
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_store_bit_exact_vs_oracle_at_model_geometry(group):
+    """8 KV heads x 128 channels, 300 tokens with outlier channels, shuffled
+    slots, a skipped token, int64 slot ids and odd (unaligned) token strides."""
+    from linkq2_b200.kernels.kv4 import materialize_kv, store_kv_quant
+    tokens, h, d, slots_total = 300, 8, 128, 512
+    k, v = ok.seeded_kv(tokens, h, d, seed=group)
+    ks = ok.static_k_scale(k)
+    g = torch.Generator().manual_seed(1)
+    slots = torch.randperm(slots_total, generator=g)[:tokens]
+    slots[7] = -1
+    ref_k, ref_v = ok.empty_pool(slots_total, h, d, group)
+    ref_k[1].copy_(ks)
+    ok.store_kv_quant(k, v, ref_k, ref_v, slots, v_group=group)
+    for pad in (0, 3):                                   # pad=3 forces the scalar-load path
+        wide_k = torch.zeros(tokens, h * d + pad, dtype=torch.float16, device="cuda")
+        wide_v = torch.zeros_like(wide_k)
+        wide_k[:, :h * d], wide_v[:, :h * d] = k.cuda().flatten(1), v.cuda().flatten(1)
+        kk = wide_k[:, :h * d].unflatten(1, (h, d))
+        vv = wide_v[:, :h * d].unflatten(1, (h, d))
+        kc, vc = ok.empty_pool(slots_total, h, d, group)
+        kc[1].copy_(ks)
+        kc, vc = cuda_pool(kc, vc, torch.uint32)
+        store_kv_quant(kk, vv, kc, vc, slots.cuda(), v_group=group)
+        assert torch.equal(words(kc[0]), ref_k[0])
+        assert torch.equal(words(vc[0]), ref_v[0])
+        assert torch.equal(vc[1].cpu(), ref_v[1])
+    sel = torch.tensor([int(slots[0]), int(slots[5]), int(slots[0]), int(slots[299])])
+    km, vm = materialize_kv(kc, vc, sel.cuda(), v_group=group)
+    rk, rv = ok.materialize_kv(ref_k, ref_v, sel, v_group=group)
+    assert torch.equal(km.cpu(), rk) and torch.equal(vm.cpu(), rv)
+    empty_k, empty_v = materialize_kv(kc, vc, torch.zeros(0, dtype=torch.int64, device="cuda"), v_group=group)
+    assert empty_k.shape == (0, h, d) and empty_v.shape == (0, h, d)
+
+
+@pytest.mark.parametrize("name", ATTN_CASES)
+def test_golden_attention(golden, name):
+    from linkq2_b200.kernels.kv4 import paged_attention_decode
+    g = golden("kv4_attention")
+    bs, m, hq, hkv, d, page, group = (int(v) for v in g[f"{name}.meta"])
+    kc = (t(g[f"{name}.kq"]).cuda(), t(g[f"{name}.ks"]).cuda())
+    vc = (t(g[f"{name}.vq"]).cuda(), t(g[f"{name}.vs"]).cuda())
+    out = paged_attention_decode(t(g[f"{name}.q"]).cuda(), kc, vc, t(g[f"{name}.table"]).cuda(),
+                                 t(g[f"{name}.lens"]).cuda(), block_n=page, num_kv_heads=hkv,
+                                 v_group=group, verify_m=m)
+    ref = t(g[f"{name}.out"]).float()
+    assert torch.isfinite(out).all()
+    assert (out.float().cpu() - ref).abs().max().item() < ATOL
+
+
+def build_case(bs, lens, m, hq, hkv, d, page, group, seed, width=None):
+    g = torch.Generator().manual_seed(seed)
+    blocks = [(l + m + page - 1) // page for l in lens]
+    n_blocks = sum(blocks) + 2
+    k, v = ok.seeded_kv(n_blocks * page, hkv, d, seed, outlier_channels=4)
+    k, v = (k.float() * 0.5).half(), (v.float() * 0.5).half()
+    kc, vc = ok.empty_pool(n_blocks * page, hkv, d, group)
+    kc[1].copy_(ok.static_k_scale(k))
+    ok.store_kv_quant(k, v, kc, vc, torch.arange(n_blocks * page), v_group=group)
+    perm = torch.randperm(n_blocks, generator=g).tolist()
+    width = width or max(blocks)
+    table = torch.full((bs, width), -1, dtype=torch.int32)
+    for i, nb in enumerate(blocks):
+        ids, perm = perm[:nb], perm[nb:]
+        table[i, :nb] = torch.tensor(ids, dtype=torch.int32)
+    q = (torch.randn(bs * m, hq, d, generator=g) * 0.5).half()
+    return kc, vc, table, torch.tensor(lens, dtype=torch.int32), q
+
+
+@pytest.mark.parametrize("bs,lens,m,hq,hkv,d,page,group", [
+    (1, [2049], 1, 32, 8, 128, 256, 64),        # long context over several splits
+    (1, [2049], 16, 32, 8, 128, 256, 64),       # 16-position verify, 64 rows per KV head
+    (3, [17, 1000, 256], 1, 16, 8, 128, 256, 64),   # Qwen3-1.7B head geometry, ragged batch
+    (2, [300, 31], 16, 16, 8, 128, 256, 64),    # verify with two row tiles
+    (2, [1, 500], 1, 4, 4, 64, 32, 32),         # no GQA, single-token context, D = 64
+    (4, [0, 5, 0, 40], 1, 8, 2, 128, 16, 128),  # empty sequences yield zeros
+    (2, [120, 64], 3, 8, 2, 128, 64, 64),       # odd verify width
+])
+def test_attention_against_oracle(bs, lens, m, hq, hkv, d, page, group):
+    from linkq2_b200.kernels.kv4 import paged_attention_decode
+    kc, vc, table, ctx, q = build_case(bs, lens, m, hq, hkv, d, page, group, seed=len(lens) + m)
+    ref = ok.paged_attention_decode(q, kc, vc, table, ctx, block_n=page, num_kv_heads=hkv,
+                                    v_group=group, verify_m=m).float()
+    gk, gv = cuda_pool(kc, vc, torch.uint32)
+    big = torch.zeros(bs * m, 2 * hq * d, dtype=torch.float16, device="cuda")
+    big[:, :hq * d] = q.cuda().flatten(1)
+    q_view = big[:, :hq * d].unflatten(1, (hq, d))          # row stride 2*HQ*D, as a fused slice
+    out = paged_attention_decode(q_view, gk, gv, table.cuda(), ctx.cuda(), block_n=page,
+                                 num_kv_heads=hkv, v_group=group, verify_m=m)
+    assert out.shape == (bs * m, hq, d) and out.is_contiguous()
+    assert torch.isfinite(out).all()
+    assert (out.float().cpu() - ref).abs().max().item() < ATOL
+    for i, length in enumerate(lens):
+        if length == 0 and m == 1:
+            assert not out[i].any()
+
+
+def test_verify_causality_bit_identical():
+    """``tests/kernels/test_kv4_verify.py:120-148`` of the reference: overwriting
+    the last draft's slot must leave every earlier row bit-identical."""
+    from linkq2_b200.kernels.kv4 import paged_attention_decode, store_kv_quant
+    bs, length, m, hq, hkv, d, page = 1, 40, 4, 4, 2, 64, 32
+    kc, vc, _, ctx, q = build_case(bs, [length], m, hq, hkv, d, page, 64, seed=3)
+    table = torch.arange(kc[0].shape[0] // page, dtype=torch.int32)[None]
+    gk, gv = cuda_pool(kc, vc)
+
+    def run():
+        return paged_attention_decode(q.cuda(), gk, gv, table.cuda(), ctx.cuda(), block_n=page,
+                                      num_kv_heads=hkv, v_group=64, verify_m=m)
+    a = run()
+    bad = (torch.randn(1, hkv, d) * 10).half().cuda()
+    store_kv_quant(bad, bad.flip(-1), gk, gv,
+                   torch.tensor([length + m - 2], dtype=torch.int32, device="cuda"), v_group=64)
+    b = run()
+    assert torch.equal(a[:m - 1], b[:m - 1]), "earlier rows changed"
+    assert not torch.equal(a[m - 1], b[m - 1]), "last row did not move"
+
+
+def test_repeated_block_and_context_swap():
+    """``tests/kernels/test_kv4_paged.py:66-115`` of the reference: a block table
+    may name one physical block twice, and each sequence uses its own length."""
+    from linkq2_b200.kernels.kv4 import paged_attention_decode
+    hq, hkv, d, page = 16, 8, 128, 128
+    k, v = ok.seeded_kv(8 * page, hkv, d, seed=0)
+    kc, vc = ok.empty_pool(8 * page, hkv, d, 64)
+    kc[1].copy_(ok.static_k_scale(k))
+    ok.store_kv_quant(k, v, kc, vc, torch.arange(8 * page), v_group=64)
+    table = torch.tensor([[1, 2, 2], [3, 4, 5]], dtype=torch.int32)
+    lens = torch.tensor([200, 300], dtype=torch.int32)
+    g = torch.Generator().manual_seed(4)
+    q = (torch.randn(2, hq, d, generator=g) * 0.5).half()
+    gk, gv = cuda_pool(kc, vc)
+    out = paged_attention_decode(q.cuda(), gk, gv, table.cuda(), lens.cuda(), block_n=page, num_kv_heads=hkv)
+    ref = ok.paged_attention_decode(q, kc, vc, table, lens, block_n=page, num_kv_heads=hkv)
+    assert (out.float().cpu() - ref.float()).abs().max().item() < ATOL
+    out2 = paged_attention_decode(q.cuda(), gk, gv, table.cuda(), lens.flip(0).cuda(), block_n=page,
+                                  num_kv_heads=hkv)
+    assert (out2[0].float() - out[0].float()).abs().max().item() > 1e-3
+    again = paged_attention_decode(q.cuda(), gk, gv, table.cuda(), lens.cuda(), block_n=page, num_kv_heads=hkv)
+    assert torch.equal(out, again)

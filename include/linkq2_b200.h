@@ -116,7 +116,8 @@ size_t lq2_kv4_attention_workspace_bytes(int batch, int verify_m, int hq, int hk
  * Paged attention over the int4 pool for one query position per sequence
  * (verify_m == 1) or verify_m consecutive positions, replacing
  * paged_attention_decode and its kernels
- * (qslab/kernels/kv4/paged_attention.py:11-150, grouped_attention.py:7-63).
+ * (qslab/kernels/kv4/paged_attention.py:11-150,
+ * qslab/kernels/kv4/grouped_attention.py:7-63).
  *
  *   q             [batch*verify_m, HQ, D] fp16, row stride q_row_stride elements
  *   block_tables  [batch, max_blocks] int32, negative entries are padding

@@ -49,6 +49,16 @@ def _load() -> ctypes.CDLL:
 
 lib = _load()
 
+# Number of kernels of this library enqueued by this process (a launch captured
+# into a CUDA graph counts once at capture and once more per replay, which the
+# graph runner adds through ``count``).
+launches = 0
+
+
+def count(n: int = 1) -> None:
+    global launches
+    launches += n
+
 
 class LinkQ2Error(RuntimeError):
     def __init__(self, status: int, where: str):

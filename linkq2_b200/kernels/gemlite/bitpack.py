@@ -23,6 +23,7 @@ def pack_w4(values: torch.Tensor, symmetric: bool) -> torch.Tensor:
         stream = torch.cuda.current_stream().cuda_stream
         _lib.check(_lib.lib.lq2_w4_pack(values.data_ptr(), 8 if symmetric else 0, packed.data_ptr(),
                                         n, k, stream), "lq2_w4_pack")
+    _lib.count()
     return packed
 
 

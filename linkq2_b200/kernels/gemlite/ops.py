@@ -47,4 +47,5 @@ def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: t
             x2.data_ptr(), x2.stride(0), packed.data_ptr(), scales.data_ptr(), zero_ptr, y.data_ptr(),
             m, n, k, group, ws.data_ptr(), ws.numel(), stream)
     _lib.check(status, "lq2_w4a16_linear")
+    _lib.count()
     return y.view(shape)

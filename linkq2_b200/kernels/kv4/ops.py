@@ -43,6 +43,7 @@ def store_kv_quant(k: torch.Tensor, v: torch.Tensor, k_cache, v_cache,
             k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), kq.data_ptr(), ks.data_ptr(),
             vq.data_ptr(), vs.data_ptr(), slots.data_ptr(), t, h, d, v_group, kq.shape[0], stream)
     _lib.check(status, "lq2_kv4_store")
+    _lib.count()
 
 
 def paged_attention_decode(q: torch.Tensor, k_cache, v_cache, block_tables: torch.Tensor,
@@ -84,6 +85,7 @@ def paged_attention_decode(q: torch.Tensor, k_cache, v_cache, block_tables: torc
             bt.data_ptr(), lens.data_ptr(), out.data_ptr(), batch, verify_m, hq, hkv, d, block_n,
             max_blocks, v_group, kq.shape[0], ws.data_ptr(), ws.numel(), stream)
     _lib.check(status, "lq2_kv4_attention")
+    _lib.count()
     return out
 
 
@@ -105,4 +107,5 @@ def materialize_kv(k_cache, v_cache, slots: torch.Tensor, v_group: int = 64):
                 kq.data_ptr(), ks.data_ptr(), vq.data_ptr(), vs.data_ptr(), slots.data_ptr(),
                 k.data_ptr(), v.data_ptr(), t, h, d, v_group, kq.shape[0], stream)
         _lib.check(status, "lq2_kv4_materialize")
+        _lib.count()
     return k, v

@@ -1,0 +1,205 @@
+"""Model runner: KV pool allocation and binding, batch preparation from pinned
+host memory, eager or CUDA-graph execution, greedy sampling.
+
+Follows ``qslab/runtime/execute/model_runner.py``: pool shapes and dtypes of
+``:146-156``, SmoothAttention / K-scale binding of ``:169-187``, decode and
+verify batch preparation of ``:262-314``, prefill preparation with the
+pool-resident prefix plan of ``:194-260``, execution and sampling of
+``:356-403``.  With tensor parallelism each rank runs the same host code on the
+same inputs and holds ``kv_heads / t`` heads of every pool tensor.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from linkq2_b200.runtime.execute.cuda_graph import CUDAGraphs
+from linkq2_b200.runtime.model.context import get_context, reset_context, set_context
+from linkq2_b200.runtime.parallel import get_tp
+from linkq2_b200.runtime.state import Sequence
+
+
+@dataclass
+class RunnerConfig:
+    kvcache_block_size: int = 256        # must be a multiple of 128 for kv4 (config.py:68-70)
+    num_kvcache_blocks: int = 0
+    v_group: int = 64
+    max_num_seqs: int = 32
+    max_model_len: int = 4096
+    enforce_eager: bool = True
+    spec_num_drafts: int = 0             # verify graphs with M = drafts + 1 rows when > 0
+
+
+class ModelRunner:
+    def __init__(self, model, config: RunnerConfig, *, smooth_kv: dict | None = None, device="cuda:0"):
+        if config.kvcache_block_size % 128:
+            raise ValueError("kv4 needs kvcache_block_size to be a multiple of 128")
+        if config.num_kvcache_blocks <= 0:
+            raise ValueError("no memory available for KV blocks")
+        self.model, self.config, self.device = model, config, torch.device(device)
+        self.block_size = config.kvcache_block_size
+        self.tp = get_tp()
+        self.graph_replays = 0
+        self.last_logits = None
+        self.allocate_kv_cache()
+        self.load_smoothing(smooth_kv)
+        self.cuda_graphs = None
+        if not config.enforce_eager:
+            self.cuda_graphs = CUDAGraphs(
+                max_batch=config.max_num_seqs, max_model_len=config.max_model_len,
+                block_size=self.block_size, hidden_size=model.config.hidden_size,
+                verify_rows=config.spec_num_drafts + 1, device=self.device)
+            self.cuda_graphs.capture(self._forward)
+
+    # ---- pool ---------------------------------------------------------------
+    def allocate_kv_cache(self):
+        cfg, mc = self.config, self.model.config
+        hkv = mc.num_key_value_heads // self.tp.size
+        d, nw, ng = mc.head_dim, mc.head_dim // 8, mc.head_dim // cfg.v_group
+        slots = cfg.num_kvcache_blocks * self.block_size
+        self.kv_cache = []
+        for _ in range(mc.num_hidden_layers):
+            kq = torch.zeros(slots, hkv, nw, dtype=torch.uint32, device=self.device)
+            ks = torch.zeros(hkv, d, dtype=torch.float16, device=self.device)
+            vq = torch.zeros(slots, hkv, nw, dtype=torch.uint32, device=self.device)
+            vs = torch.zeros(slots, hkv, ng, dtype=torch.float16, device=self.device)
+            self.kv_cache.append(((kq, ks), (vq, vs)))
+        layer_id = 0
+        for module in self.model.modules():
+            if hasattr(module, "k_cache") and hasattr(module, "v_cache"):
+                module.k_cache, module.v_cache = self.kv_cache[layer_id]
+                module.v_group, module.block_n, module.kv_cache_dtype = cfg.v_group, self.block_size, 'kv4'
+                layer_id += 1
+
+    def load_smoothing(self, ck: dict | None):
+        """``{'lambda': [L, HKV, D], 'kscale': [L, HKV, D]}`` over all KV heads;
+        each rank keeps its heads.  KV4 requires a calibration (config.py:64-65)."""
+        if ck is None:
+            raise ValueError("the KV4 cache needs a SmoothAttention / K-scale calibration")
+        mc = self.model.config
+        expected = (mc.num_hidden_layers, mc.num_key_value_heads, mc.head_dim)
+        lam, kscale = ck["lambda"].float(), ck["kscale"].float()
+        for name, tensor in (("lambda", lam), ("kscale", kscale)):
+            stored = tensor.half()
+            if tuple(tensor.shape) != expected or not torch.isfinite(stored).all() or (stored <= 0).any():
+                raise ValueError(f"{name} must have shape {expected} and finite positive FP16 values")
+        hkv = mc.num_key_value_heads // self.tp.size
+        heads = slice(self.tp.rank * hkv, (self.tp.rank + 1) * hkv)
+        unit = bool((lam == 1).all())
+        layer_id = 0
+        for module in self.model.modules():
+            if hasattr(module, "k_cache") and hasattr(module, "v_cache"):
+                if not unit:
+                    module.set_smooth_lambda(lam[layer_id, heads].to(self.device))
+                module.k_cache[1].copy_(kscale[layer_id, heads].half())
+                layer_id += 1
+
+    # ---- batch preparation ----------------------------------------------------
+    def _h2d(self, data, dtype):
+        return torch.tensor(data, dtype=dtype, pin_memory=True).to(self.device, non_blocking=True)
+
+    def prepare_block_tables(self, seqs):
+        width = max(len(seq.block_table) for seq in seqs)
+        return self._h2d([seq.block_table + [-1] * (width - len(seq.block_table)) for seq in seqs], torch.int32)
+
+    def prepare_decode(self, seqs: list[Sequence]):
+        input_ids = self._h2d([seq.last_token for seq in seqs], torch.int64)
+        positions = self._h2d([len(seq) - 1 for seq in seqs], torch.int64)
+        slot_mapping = self._h2d([seq.slot(len(seq) - 1) for seq in seqs], torch.int32)
+        context_lens = self._h2d([len(seq) for seq in seqs], torch.int32)
+        set_context(False, slot_mapping=slot_mapping, context_lens=context_lens,
+                    block_tables=self.prepare_block_tables(seqs))
+        return input_ids, positions
+
+    def prepare_verify(self, seqs: list[Sequence], drafts: list[list[int]]):
+        """M = drafts + 1 rows per sequence: [last committed token, drafts...]; row m
+        is position L-1+m and reads keys [0, L+m) (model_runner.py:285-314)."""
+        gamma = self.config.spec_num_drafts
+        m_rows = gamma + 1
+        ids, pos, slots, lens = [], [], [], []
+        for seq, d in zip(seqs, drafts):
+            length = len(seq)
+            d = list(d)[:gamma]
+            ids.extend([seq.last_token] + d + [0] * (gamma - len(d)))
+            pos.extend(range(length - 1, length + gamma))
+            lens.append(length)
+            for m in range(m_rows):
+                p = length - 1 + m
+                ok = m <= len(d) and p // self.block_size < len(seq.block_table)
+                slots.append(seq.slot(p) if ok else -1)
+        set_context(False, slot_mapping=self._h2d(slots, torch.int32), context_lens=self._h2d(lens, torch.int32),
+                    block_tables=self.prepare_block_tables(seqs), verify_m=m_rows)
+        return self._h2d(ids, torch.int64), self._h2d(pos, torch.int64)
+
+    def prepare_prefill(self, seqs: list[Sequence], counts: list[int]):
+        """Schedule ``counts[i]`` prompt tokens of each sequence after its cached prefix."""
+        ids, pos, slots, cu_q, cu_k = [], [], [], [0], [0]
+        prefix_slots, plan, q_off = [], [], 0
+        for seq, n in zip(seqs, counts):
+            start, end = seq.num_cached_tokens, seq.num_cached_tokens + n
+            ids.extend(seq.token_ids[start:end])
+            pos.extend(range(start, end))
+            slots.extend(seq.slot(p) for p in range(start, end))
+            cu_q.append(cu_q[-1] + n)
+            cu_k.append(cu_k[-1] + end)
+            plan.append((len(prefix_slots), start, q_off, q_off + n, True))
+            prefix_slots.extend(seq.slot(p) for p in range(start))
+            q_off += n
+        has_prefix = cu_k[-1] > cu_q[-1]
+        set_context(True, self._h2d(cu_q, torch.int32), self._h2d(cu_k, torch.int32),
+                    max(counts), max(c[1] + (c[3] - c[2]) for c in plan),
+                    self._h2d(slots, torch.int32), None,
+                    self.prepare_block_tables(seqs) if has_prefix else None,
+                    prefix_slots=self._h2d(prefix_slots, torch.int64) if has_prefix else None,
+                    prefix_plan=plan if has_prefix else None)
+        return self._h2d(ids, torch.int64), self._h2d(pos, torch.int64)
+
+    # ---- execution ------------------------------------------------------------
+    def _forward(self, input_ids, positions):
+        return self.model(input_ids, positions)
+
+    @torch.inference_mode()
+    def run_model(self, input_ids, positions, is_prefill, *, rows=1):
+        graphs = self.cuda_graphs
+        if is_prefill or graphs is None or input_ids.size(0) // rows > max(graphs.batch_sizes) \
+                or rows not in graphs.families:
+            return self._forward(input_ids, positions)
+        self.graph_replays += 1
+        return graphs.replay(input_ids, positions, get_context(), rows)
+
+    @torch.inference_mode()
+    def run(self, seqs: list[Sequence], is_prefill: bool, counts: list[int] | None = None) -> list[int]:
+        """One step; returns one greedy token per sequence (for prefill: the token
+        after the last scheduled position)."""
+        if is_prefill:
+            counts = counts or [len(s) - s.num_cached_tokens for s in seqs]
+            input_ids, positions = self.prepare_prefill(seqs, counts)
+        else:
+            input_ids, positions = self.prepare_decode(seqs)
+        hidden = self.run_model(input_ids, positions, is_prefill)
+        if is_prefill:
+            hidden = hidden[(get_context().cu_seqlens_q[1:] - 1).long()]
+            for seq, n in zip(seqs, counts):
+                seq.num_cached_tokens += n
+        self.last_logits = self.model.compute_logits(hidden)
+        tokens = self.last_logits.argmax(dim=-1).tolist()
+        reset_context()
+        return tokens
+
+    @torch.inference_mode()
+    def verify(self, seqs: list[Sequence], drafts: list[list[int]]) -> list[list[int]]:
+        """One M-row verify forward; returns the greedy token at every row."""
+        m_rows = self.config.spec_num_drafts + 1
+        input_ids, positions = self.prepare_verify(seqs, drafts)
+        hidden = self.run_model(input_ids, positions, False, rows=m_rows)
+        tokens = self.model.compute_logits(hidden).argmax(dim=-1).view(len(seqs), m_rows).tolist()
+        reset_context()
+        return tokens
+
+
+def amax_calibration(num_layers: int, num_kv_heads: int, head_dim: int, kscale: float = 0.3) -> dict:
+    """Unit-lambda calibration with a constant K scale, the form the reference's
+    test fixture writes (``tests/conftest.py:41-43``)."""
+    return {"lambda": torch.ones(num_layers, num_kv_heads, head_dim),
+            "kscale": torch.full((num_layers, num_kv_heads, head_dim), kscale)}

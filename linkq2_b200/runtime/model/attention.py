@@ -1,0 +1,85 @@
+"""One attention layer's interface into the int4 paged KV pool.
+
+Mirror of ``PagedAttention`` (``qslab/runtime/model/attention.py:21-144``) for
+the KV4 cache: SmoothAttention scaling, store before attention, paged decode /
+verify through the KV4 kernels, and prefill over the fp16 rows of the step with
+the pool-resident prefix restored in front of them.  The reference runs prefill
+through the flash-attn wheel (``attention.py:121-131``); here it is torch's
+scaled_dot_product_attention per sequence — prefill attention is not part of
+the replaced path.  ``num_heads`` / ``num_kv_heads`` are this rank's shard.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from linkq2_b200.kernels.kv4 import materialize_kv, paged_attention_decode, store_kv_quant
+from linkq2_b200.runtime.model.context import get_context
+
+
+class PagedAttention(nn.Module):
+    def __init__(self, num_heads: int, head_dim: int, scale: float, num_kv_heads: int,
+                 block_n: int = 128, v_group: int = 64):
+        super().__init__()
+        self.num_heads, self.head_dim, self.scale = num_heads, head_dim, scale
+        self.num_kv_heads = num_kv_heads
+        self.block_n, self.v_group = block_n, v_group
+        self.k_cache = self.v_cache = None      # (packed, scales) tuples
+        self.kv_cache_dtype = 'kv4'
+        self.lam = None                         # [H_kv, D] SmoothAttention
+        self.lam_q = None                       # [H_q, D] expanded over each GQA group
+
+    def set_smooth_lambda(self, lam: torch.Tensor):
+        self.lam = lam
+        rep = self.num_heads // self.num_kv_heads
+        self.lam_q = lam.repeat_interleave(rep, dim=0).contiguous()
+
+    def _prefill(self, ctx, q, k, v):
+        out = torch.empty_like(q)
+        if ctx.block_tables is not None and ctx.prefix_plan:
+            kp, vp = materialize_kv(self.k_cache, self.v_cache, ctx.prefix_slots, v_group=self.v_group)
+            plan = ctx.prefix_plan
+        else:
+            cu = ctx.cu_seqlens_q.tolist()
+            kp = vp = None
+            plan = [(0, 0, cu[i], cu[i + 1], True) for i in range(len(cu) - 1)]
+        for slot_off, cached, q0, q1, is_prefill in plan:
+            ks, vs = [], []
+            if cached > 0:
+                ks.append(kp[slot_off:slot_off + cached])
+                vs.append(vp[slot_off:slot_off + cached])
+            if is_prefill:
+                ks.append(k[q0:q1])
+                vs.append(v[q0:q1])
+            kk, vv = torch.cat(ks), torch.cat(vs)
+            tq, tk = q1 - q0, kk.shape[0]
+            # bottom-right aligned causal mask: query i sees keys [0, tk - tq + i]
+            mask = torch.ones(tq, tk, dtype=torch.bool, device=q.device).tril(diagonal=tk - tq)
+            o = F.scaled_dot_product_attention(
+                q[q0:q1].transpose(0, 1).unsqueeze(0), kk.transpose(0, 1).unsqueeze(0),
+                vv.transpose(0, 1).unsqueeze(0), attn_mask=mask, scale=self.scale, enable_gqa=True)
+            out[q0:q1] = o.squeeze(0).transpose(0, 1)
+        return out
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        ctx = get_context()
+        if self.kv_cache_dtype != 'kv4':
+            raise NotImplementedError("this package implements the KV4 cache path only")
+        if self.lam is not None:
+            q = q * self.lam_q.to(q.dtype)
+            k = k / self.lam.to(k.dtype)
+        k_cache, v_cache = self.k_cache, self.v_cache
+        # store first: decode's context_lens includes the token being processed
+        if k_cache is not None and v_cache is not None and k.shape[0] > 0:
+            store_kv_quant(k.view(-1, self.num_kv_heads, self.head_dim),
+                           v.view(-1, self.num_kv_heads, self.head_dim),
+                           k_cache, v_cache, ctx.slot_mapping.view(-1), v_group=self.v_group)
+        if ctx.is_prefill:
+            return self._prefill(ctx, q.view(-1, self.num_heads, self.head_dim),
+                                 k.view(-1, self.num_kv_heads, self.head_dim),
+                                 v.view(-1, self.num_kv_heads, self.head_dim))
+        assert k_cache is not None and v_cache is not None
+        return paged_attention_decode(q, k_cache, v_cache, ctx.block_tables, ctx.context_lens,
+                                      block_n=self.block_n, num_kv_heads=self.num_kv_heads,
+                                      k_scale=k_cache[1], v_group=self.v_group, verify_m=ctx.verify_m)

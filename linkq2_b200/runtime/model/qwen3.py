@@ -1,0 +1,155 @@
+"""Qwen3 decoder with W4-swappable projections, int4 paged attention and a
+tensor-parallel split.
+
+Layer graph and module names follow ``qslab/runtime/model/qwen3.py:18-137`` (and
+the HF checkpoint): separate q/k/v/gate/up projections, q/k RMSNorm, RoPE,
+residual-fused RMSNorm.  Under tensor parallelism every rank holds
+``heads / t`` query heads, ``kv_heads / t`` KV heads and ``intermediate / t``
+MLP channels; ``o_proj`` and ``down_proj`` produce partial sums that are
+all-reduced.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from linkq2_b200.runtime.model.attention import PagedAttention
+from linkq2_b200.runtime.model.primitives import Linear, LMHead, RMSNorm, VocabEmbedding
+from linkq2_b200.runtime.model.rotary import RotaryEmbedding
+from linkq2_b200.runtime.parallel import get_tp
+
+
+@dataclass
+class ModelConfig:
+    """The fields of a HF ``Qwen3Config`` this runtime reads."""
+    vocab_size: int = 151936
+    hidden_size: int = 4096
+    intermediate_size: int = 12288
+    num_hidden_layers: int = 36
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+    max_position_embeddings: int = 40960
+    tie_word_embeddings: bool = False
+
+    @classmethod
+    def from_dict(cls, cfg: dict) -> "ModelConfig":
+        fields = {f: cfg[f] for f in cls.__dataclass_fields__ if f in cfg}
+        if "head_dim" not in fields:
+            fields["head_dim"] = cfg["hidden_size"] // cfg["num_attention_heads"]
+        if "rope_theta" not in fields and isinstance(cfg.get("rope_parameters"), dict):
+            fields["rope_theta"] = cfg["rope_parameters"].get("rope_theta", 1e6)
+        return cls(**fields)
+
+    @classmethod
+    def qwen3_8b(cls):
+        return cls()
+
+    @classmethod
+    def qwen3_1p7b(cls):
+        return cls(hidden_size=2048, intermediate_size=6144, num_hidden_layers=28,
+                   num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                   tie_word_embeddings=True)
+
+
+class Qwen3Attention(nn.Module):
+    def __init__(self, config: ModelConfig, rope: RotaryEmbedding):
+        super().__init__()
+        tp = get_tp()
+        self.tp = tp
+        self.num_heads = config.num_attention_heads // tp.size
+        self.num_kv_heads = config.num_key_value_heads // tp.size
+        self.head_dim = config.head_dim
+        self.q_size = self.num_heads * self.head_dim
+        self.kv_size = self.num_kv_heads * self.head_dim
+        self.q_proj = Linear(config.hidden_size, self.q_size)
+        self.k_proj = Linear(config.hidden_size, self.kv_size)
+        self.v_proj = Linear(config.hidden_size, self.kv_size)
+        self.o_proj = Linear(self.q_size, config.hidden_size)
+        self.rotary_emb = rope
+        self.attn = PagedAttention(self.num_heads, self.head_dim, self.head_dim ** -0.5, self.num_kv_heads)
+        self.q_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+        self.k_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+
+    def forward(self, positions, hidden_states):
+        q = self.q_proj(hidden_states).view(-1, self.num_heads, self.head_dim)
+        k = self.k_proj(hidden_states).view(-1, self.num_kv_heads, self.head_dim)
+        v = self.v_proj(hidden_states).view(-1, self.num_kv_heads, self.head_dim)
+        q, k = self.q_norm(q), self.k_norm(k)
+        q, k = self.rotary_emb(positions, q, k)
+        o = self.attn(q, k, v)
+        return self.tp.all_reduce(self.o_proj(o.flatten(1, -1)))
+
+
+class Qwen3MLP(nn.Module):
+    def __init__(self, config: ModelConfig):
+        super().__init__()
+        tp = get_tp()
+        self.tp = tp
+        inter = config.intermediate_size // tp.size
+        self.gate_proj = Linear(config.hidden_size, inter)
+        self.up_proj = Linear(config.hidden_size, inter)
+        self.down_proj = Linear(inter, config.hidden_size)
+
+    def forward(self, x):
+        return self.tp.all_reduce(self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x)))
+
+
+class Qwen3DecoderLayer(nn.Module):
+    def __init__(self, config: ModelConfig, rope: RotaryEmbedding):
+        super().__init__()
+        self.self_attn = Qwen3Attention(config, rope)
+        self.mlp = Qwen3MLP(config)
+        self.input_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, positions, hidden_states, residual):
+        if residual is None:
+            hidden_states, residual = self.input_layernorm(hidden_states), hidden_states
+        else:
+            hidden_states, residual = self.input_layernorm(hidden_states, residual)
+        hidden_states = self.self_attn(positions, hidden_states)
+        hidden_states, residual = self.post_attention_layernorm(hidden_states, residual)
+        return self.mlp(hidden_states), residual
+
+
+class Qwen3Model(nn.Module):
+    def __init__(self, config: ModelConfig, max_position: int | None = None, device=None):
+        super().__init__()
+        rope = RotaryEmbedding(config.head_dim, max_position or config.max_position_embeddings,
+                               config.rope_theta, device=device)
+        self.embed_tokens = VocabEmbedding(config.vocab_size, config.hidden_size)
+        self.layers = nn.ModuleList([Qwen3DecoderLayer(config, rope) for _ in range(config.num_hidden_layers)])
+        self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, input_ids, positions):
+        hidden_states, residual = self.embed_tokens(input_ids), None
+        for layer in self.layers:
+            hidden_states, residual = layer(positions, hidden_states, residual)
+        hidden_states, _ = self.norm(hidden_states, residual)
+        return hidden_states
+
+
+class Qwen3ForCausalLM(nn.Module):
+    # module-name suffix -> how its weight is split across tensor-parallel ranks
+    TP_SPLIT = {"q_proj": "column", "k_proj": "column", "v_proj": "column", "gate_proj": "column",
+                "up_proj": "column", "o_proj": "row", "down_proj": "row"}
+
+    def __init__(self, config: ModelConfig, max_position: int | None = None, device=None):
+        super().__init__()
+        self.config = config
+        self.model = Qwen3Model(config, max_position, device)
+        self.lm_head = LMHead(config.vocab_size, config.hidden_size)
+        if config.tie_word_embeddings:
+            self.lm_head.weight = self.model.embed_tokens.weight
+
+    def forward(self, input_ids, positions):
+        return self.model(input_ids, positions)
+
+    def compute_logits(self, hidden_states):
+        return self.lm_head(hidden_states)

@@ -27,6 +27,7 @@ extern "C" {
 #define LQ2_ERR_ALIGN 3      /* pointer or stride misaligned for vector access */
 #define LQ2_ERR_WORKSPACE 4  /* workspace missing or smaller than *_workspace_bytes */
 #define LQ2_ERR_CUDA 5       /* the launch itself was refused by the CUDA runtime */
+#define LQ2_ERR_LIMIT 6      /* lq2_kv4_attention_static: scratch need exceeds the built-in buffer */
 
 /* Human-readable text for a status code. */
 const char* lq2_status_string(int status);
@@ -135,6 +136,39 @@ int lq2_kv4_attention(const void* q, int64_t q_row_stride, const uint32_t* kq, c
                       const int32_t* context_lens, void* out, int batch, int verify_m, int hq,
                       int hkv, int d, int page, int max_blocks, int v_group, int64_t num_slots,
                       void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * lq2_kv4_attention for callers that cannot allocate device memory.  It has no
+ * counterpart in the reference.
+ *
+ * Some hosts of this library never get to call cudaMalloc: a plugin loaded into
+ * a serving process that owns the whole device through its own pool and passes
+ * the plugin nothing but the request's tensors, or code that runs where an
+ * allocation would stall the device or is forbidden outright.  For them the
+ * split partials and ticket counters live in a 16 MiB array compiled into the
+ * library (lq2_kv4_attention_static_max_bytes() returns the size); every GPU
+ * that loads the library keeps that array until the process exits.  Arguments
+ * and results are those of lq2_kv4_attention without the workspace pair; the
+ * same kernel runs, so the output is identical.
+ *
+ *  - A problem whose lq2_kv4_attention_workspace_bytes() exceeds the array is
+ *    refused with LQ2_ERR_LIMIT and launches nothing.
+ *  - The first call on each device looks up the array's device address; make
+ *    that first call outside any stream capture.
+ *  - All calls on a device share the one array.  Each call clears the counters
+ *    it uses on its stream before the kernel, so calls issued one after another
+ *    are independent, but two calls that may run at the same time on one GPU
+ *    (different streams) race on it.
+ *  - The call itself performs no cudaMalloc, cudaFree or other allocation.
+ */
+int lq2_kv4_attention_static(const void* q, int64_t q_row_stride, const uint32_t* kq, const void* ks,
+                             const uint32_t* vq, const void* vs, const int32_t* block_tables,
+                             const int32_t* context_lens, void* out, int batch, int verify_m, int hq,
+                             int hkv, int d, int page, int max_blocks, int v_group,
+                             int64_t num_slots, void* stream);
+
+/* Size in bytes of the array behind lq2_kv4_attention_static. */
+size_t lq2_kv4_attention_static_max_bytes(void);
 
 /*
  * Prefix restore: gather the given slots and dequantise them to fp16

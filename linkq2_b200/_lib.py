@@ -13,7 +13,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "liblinkq2_b200.so"
 
 OK = 0
-ERR_ARG, ERR_SHAPE, ERR_ALIGN, ERR_WORKSPACE, ERR_CUDA = 1, 2, 3, 4, 5
+ERR_ARG, ERR_SHAPE, ERR_ALIGN, ERR_WORKSPACE, ERR_CUDA, ERR_LIMIT = 1, 2, 3, 4, 5, 6
 
 # name -> (restype, argtypes); mirrors include/linkq2_b200.h one to one
 SIGNATURES = {
@@ -30,6 +30,10 @@ SIGNATURES = {
     "lq2_kv4_attention": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                   c_int, c_int64, c_void_p, c_size_t, c_void_p]),
+    "lq2_kv4_attention_static": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                                         c_int, c_int, c_int64, c_void_p]),
+    "lq2_kv4_attention_static_max_bytes": (c_size_t, []),
     "lq2_kv4_materialize": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p]),
 }

@@ -16,6 +16,9 @@ size_t kv4_attention_workspace_bytes(int, int, int, int, int, int, int);
 int kv4_attention_launch(const __half*, int64_t, const uint32_t*, const __half*, const uint32_t*,
                          const __half*, const int32_t*, const int32_t*, __half*, int, int, int, int, int,
                          int, int, int, int64_t, void*, size_t, cudaStream_t);
+size_t kv4_attention_builtin_scratch_bytes();
+int kv4_attention_builtin_scratch(void**);
+size_t kv4_attention_counter_bytes(int, int);
 }  // namespace lq2
 
 using namespace lq2;
@@ -41,6 +44,7 @@ const char* lq2_status_string(int status) {
         case LQ2_ERR_ALIGN: return "pointer or stride not aligned for vector access";
         case LQ2_ERR_WORKSPACE: return "workspace missing or too small";
         case LQ2_ERR_CUDA: return "CUDA launch failed";
+        case LQ2_ERR_LIMIT: return "problem needs more scratch than the built-in 16 MiB buffer";
         default: return "unknown status";
     }
 }
@@ -113,6 +117,34 @@ int lq2_kv4_attention(const void* q, int64_t q_row_stride, const uint32_t* kq, c
                                 block_tables, context_lens, static_cast<__half*>(out), batch, verify_m, hq,
                                 hkv, d, page, max_blocks, v_group, num_slots, workspace, workspace_bytes,
                                 static_cast<cudaStream_t>(stream));
+}
+
+size_t lq2_kv4_attention_static_max_bytes(void) { return kv4_attention_builtin_scratch_bytes(); }
+
+int lq2_kv4_attention_static(const void* q, int64_t q_row_stride, const uint32_t* kq, const void* ks,
+                             const uint32_t* vq, const void* vs, const int32_t* block_tables,
+                             const int32_t* context_lens, void* out, int batch, int verify_m, int hq,
+                             int hkv, int d, int page, int max_blocks, int v_group, int64_t num_slots,
+                             void* stream) {
+    if (batch == 0) return LQ2_OK;
+    if (!attn_shape_ok(batch, verify_m, hq, hkv, d, page, max_blocks)) return LQ2_ERR_SHAPE;
+    if (v_group < d / 8 || !pow2(v_group) || d % v_group || num_slots <= 0 || num_slots % page) return LQ2_ERR_SHAPE;
+    const size_t need = kv4_attention_workspace_bytes(batch, verify_m, hq, hkv, d, page, max_blocks);
+    if (need > kv4_attention_builtin_scratch_bytes()) return LQ2_ERR_LIMIT;
+    if (!q || !kq || !ks || !vq || !vs || !block_tables || !context_lens || !out) return LQ2_ERR_ARG;
+    if (!aligned(kq, 16) || !aligned(vq, 16) || !aligned(q, 2)) return LQ2_ERR_ALIGN;
+    void* scratch = nullptr;
+    const int st = kv4_attention_builtin_scratch(&scratch);
+    if (st != LQ2_OK) return st;
+    // The array keeps whatever the previous call left; the ticket counters must
+    // start at zero, so clear the ones this call will use (a stream-ordered
+    // memset, not an allocation).
+    if (cudaMemsetAsync(scratch, 0, kv4_attention_counter_bytes(batch, hkv),
+                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return LQ2_ERR_CUDA;
+    return lq2_kv4_attention(q, q_row_stride, kq, ks, vq, vs, block_tables, context_lens, out, batch,
+                             verify_m, hq, hkv, d, page, max_blocks, v_group, num_slots, scratch,
+                             kv4_attention_builtin_scratch_bytes(), stream);
 }
 
 int lq2_kv4_materialize(const uint32_t* kq, const void* ks, const uint32_t* vq, const void* vs,

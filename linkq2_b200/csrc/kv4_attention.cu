@@ -25,7 +25,17 @@
 // (sequence, KV head) merges the partials in split order and writes fp16.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
+
+// Built-in scratch for lq2_kv4_attention_static: callers that cannot allocate
+// device memory get the split partials and ticket counters from this array
+// instead of a workspace argument.  Every device that loads the library holds
+// these 16 MiB until the process exits.  In host code the symbol below is only a
+// handle; its device address is resolved per device with cudaGetSymbolAddress.
+#define LQ2_BUILTIN_SCRATCH_BYTES (size_t(16) << 20)
+static __device__ __align__(256) unsigned char g_lq2_attention_scratch[LQ2_BUILTIN_SCRATCH_BYTES];
 
 namespace lq2 {
 
@@ -380,6 +390,29 @@ size_t kv4_attention_workspace_bytes(int batch, int m, int hq, int hkv, int d, i
     if (splits > 1) bytes += size_t(batch) * hq * m * splits * (d + 2) * sizeof(float);
     return bytes;
 }
+
+size_t kv4_attention_builtin_scratch_bytes() { return LQ2_BUILTIN_SCRATCH_BYTES; }
+
+// Device address of the built-in scratch on the current device, resolved on the
+// first call per device (this may load the module, so it must not happen while
+// a stream is being captured) and remembered afterwards.
+int kv4_attention_builtin_scratch(void** out) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static void* addr[kMaxDevices] = {};
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return LQ2_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_lq2_attention_scratch) != cudaSuccess || !p) return LQ2_ERR_CUDA;
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return LQ2_OK;
+}
+
+size_t kv4_attention_counter_bytes(int batch, int hkv) { return size_t(batch) * hkv * sizeof(int); }
 
 int kv4_attention_launch(const __half* q, int64_t q_stride, const uint32_t* kq, const __half* ks,
                          const uint32_t* vq, const __half* vs, const int32_t* bt, const int32_t* lens,

@@ -271,6 +271,8 @@ def run_b200(args):
     launches_before = _lib.launches
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.profile_range:
+        torch.cuda.profiler.start()
     with torch.inference_mode():
         ev0.record()
         for i in range(steps):
@@ -281,6 +283,8 @@ def run_b200(args):
             history[i] = ids
         ev1.record()
     barrier()
+    if args.profile_range:
+        torch.cuda.profiler.stop()
     ms_value = max_over_ranks(ev0.elapsed_time(ev1))
     launches = _lib.launches - launches_before
     clocks = sampler.stop() if sampler else None
@@ -376,6 +380,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket the timed decode steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -52,10 +52,11 @@ int lq2_abi_version(void);
 int lq2_w4_pack(const int8_t* values, int offset, int32_t* packed, int n, int k, void* stream);
 
 /*
- * Bytes of scratch lq2_w4a16_linear needs for this problem size (0 is possible).
- * The buffer must be zero-filled once when it is created; each call leaves it
- * zero-filled again where it needs zeros, so it can be reused by later calls on
- * the same stream.  Two calls that may overlap on the GPU need two buffers.
+ * Bytes of scratch lq2_w4a16_linear needs for this problem size.  The current
+ * kernels keep split-K partials on chip and need none (the answer is 0 and the
+ * workspace argument may be NULL); the query stays in the ABI so that a caller
+ * written against it keeps working if a later kernel needs scratch again.  A
+ * non-empty buffer must be zero-filled once when it is created.
  */
 size_t lq2_w4a16_workspace_bytes(int m, int n, int k);
 
@@ -73,7 +74,7 @@ size_t lq2_w4a16_workspace_bytes(int m, int n, int k);
  *              symmetric scalar zero 8
  *   y          [M, N] fp16 contiguous
  *   group      power of two >= 32 dividing K;  N a multiple of 32
- *   workspace  lq2_w4a16_workspace_bytes(M, N, K) bytes (see above)
+ *   workspace  lq2_w4a16_workspace_bytes(M, N, K) bytes (see above); NULL when that is 0
  * Products are accumulated in fp32 and rounded to fp16 once.
  */
 int lq2_w4a16_linear(const void* x, int64_t x_row_stride, const int32_t* packed,
@@ -179,6 +180,55 @@ size_t lq2_kv4_attention_static_max_bytes(void);
 int lq2_kv4_materialize(const uint32_t* kq, const void* ks, const uint32_t* vq, const void* vs,
                         const int64_t* slots, void* k_out, void* v_out, int tokens, int hkv,
                         int d, int v_group, int64_t num_slots, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Fused elementwise steps between the operators above.  The reference runs
+ * them as eager torch kernels; these keep its rounding points (fp32 statistics
+ * and rotation, fp16 casts and fp16 products where torch has them).
+ * -------------------------------------------------------------------------- */
+
+/*
+ * RMSNorm with optional residual add, replacing RMSNorm.forward
+ * (qslab/runtime/model/primitives.py:15-36).
+ *   residual == NULL:  out = fp16(x32 * rsqrt(mean(x32^2) + eps)) * weight
+ *   residual != NULL:  s = fp32(x) + fp32(residual); residual_out = fp16(s);
+ *                      out = fp16(s * rsqrt(mean(s^2) + eps)) * weight
+ * x [rows, hidden] fp16 with row stride x_row_stride; residual, out,
+ * residual_out contiguous [rows, hidden]; residual_out may alias residual.
+ * hidden a multiple of 8, at most 8192.
+ */
+int lq2_rmsnorm(const void* x, int64_t x_row_stride, const void* residual, const void* weight,
+                void* out, void* residual_out, int rows, int hidden, float eps, void* stream);
+
+/*
+ * out = fp16(silu(fp32(gate))) * up, replacing F.silu(gate) * up of Qwen3MLP.forward
+ * (qslab/runtime/model/qwen3.py:64).  gate/up [rows, width] fp16 with row
+ * strides; out contiguous.
+ */
+int lq2_silu_mul(const void* gate, int64_t gate_row_stride, const void* up, int64_t up_row_stride,
+                 void* out, int rows, int width, void* stream);
+
+/*
+ * Everything between the q/k/v projections and the attention kernel in one
+ * launch: per-head RMSNorm of q and k, rotary embedding, SmoothAttention scaling
+ * and the KV4 store, replacing qslab/runtime/model/qwen3.py:49-51,
+ * rotary.py:12-16,103-108, attention.py:72-77 and :102-110 (store_kv_quant).
+ *   q [T, HQ, D], k, v [T, HKV, D] fp16, token strides in elements, head stride D
+ *   q_norm_weight, k_norm_weight [D] fp16;  cos_sin [max_pos, D] fp32, cos in
+ *   the first D/2 columns and sin in the last (the reference's cos_sin_cache);
+ *   positions [T] int64;  lam_q [HQ, D], lam_k [HKV, D] fp16 or NULL (lambda = 1)
+ *   q_out [T, HQ, D] fp16 contiguous;  k_out [T, HKV, D] fp16 or NULL: the
+ *   rotated, scaled keys for callers that also need them in fp16 (prefill)
+ *   kq, ks, vq, vs, slots, v_group, num_slots as in lq2_kv4_store; slots == NULL
+ *   skips the store.
+ * The cache bytes equal lq2_kv4_store applied to (k_out, v).  D is 64 or 128.
+ */
+int lq2_pre_attention(const void* q, const void* k, const void* v, int64_t q_stride, int64_t k_stride,
+                      int64_t v_stride, const void* q_norm_weight, const void* k_norm_weight,
+                      const float* cos_sin, const int64_t* positions, const void* lam_q,
+                      const void* lam_k, void* q_out, void* k_out, uint32_t* kq, const void* ks,
+                      uint32_t* vq, void* vs, const int32_t* slots, int tokens, int hq, int hkv, int d,
+                      int v_group, int64_t num_slots, float eps, void* stream);
 
 #ifdef __cplusplus
 }

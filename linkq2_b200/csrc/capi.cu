@@ -69,7 +69,7 @@ int lq2_w4a16_linear(const void* x, int64_t x_row_stride, const int32_t* packed,
     if (!x || !packed || !scales || !y) return LQ2_ERR_ARG;
     if (!w4_shape_ok(m, n, k, group)) return m <= 0 || n <= 0 || k <= 0 ? LQ2_ERR_ARG : LQ2_ERR_SHAPE;
     if (!aligned(x, 16) || x_row_stride % 8 || x_row_stride < k || !aligned(packed, 16) ||
-        !aligned(scales, 8) || (zeros && !aligned(zeros, 8)) || !aligned(y, 8) || !aligned(workspace, 16))
+        !aligned(scales, 16) || (zeros && !aligned(zeros, 16)) || !aligned(y, 8))
         return LQ2_ERR_ALIGN;
     return w4a16_stream_launch(static_cast<const __half*>(x), x_row_stride, packed,
                                static_cast<const __half*>(scales), static_cast<const __half*>(zeros),

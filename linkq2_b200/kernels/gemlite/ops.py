@@ -41,11 +41,11 @@ def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: t
     zero_ptr = None if zeros.numel() == 1 else zeros.data_ptr()
     with torch.cuda.device(x.device):
         need = _lib.lib.lq2_w4a16_workspace_bytes(m, n, k)
-        ws = _workspace.get("w4a16", need, x.device)
+        ws = _workspace.get("w4a16", need, x.device) if need else None
         stream = torch.cuda.current_stream().cuda_stream
         status = _lib.lib.lq2_w4a16_linear(
             x2.data_ptr(), x2.stride(0), packed.data_ptr(), scales.data_ptr(), zero_ptr, y.data_ptr(),
-            m, n, k, group, ws.data_ptr(), ws.numel(), stream)
+            m, n, k, group, ws.data_ptr() if need else None, ws.numel() if need else 0, stream)
     _lib.check(status, "lq2_w4a16_linear")
     _lib.count()
     return y.view(shape)

@@ -41,6 +41,7 @@ class CUDAGraphs:
         self.families: dict[int, GraphFamily] = {}
         self.kernels_per_graph: dict[tuple, int] = {}
         self.pool = None
+        self.stream = torch.cuda.Stream(device=device)
 
     @torch.inference_mode()
     def capture(self, forward):
@@ -56,17 +57,22 @@ class CUDAGraphs:
                 outputs=torch.zeros(size, self.hidden_size, dtype=torch.float16, device=dev),
             )
             graphs = {}
+            # Warm-up and capture run on one side stream: the kernels' scratch
+            # buffers are cached per stream, so the eager pass creates exactly the
+            # buffers the captured launches then reuse.
+            stream = self.stream
             for batch in reversed(self.batch_sizes):
                 count = batch * rows
                 graph = torch.cuda.CUDAGraph()
                 set_context(False, slot_mapping=buffers['slot_mapping'][:count],
                             context_lens=buffers['context_lens'][:batch],
                             block_tables=buffers['block_tables'][:batch], verify_m=rows)
-                # eager warm-up: creates the kernels' cached workspaces outside capture
-                buffers['outputs'][:count] = forward(buffers['input_ids'][:count], buffers['positions'][:count])
+                stream.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(stream):
+                    buffers['outputs'][:count] = forward(buffers['input_ids'][:count], buffers['positions'][:count])
                 torch.cuda.synchronize()
                 before = _lib.launches
-                with torch.cuda.graph(graph, self.pool):
+                with torch.cuda.graph(graph, self.pool, stream=stream):
                     buffers['outputs'][:count] = forward(buffers['input_ids'][:count],
                                                          buffers['positions'][:count])
                 self.kernels_per_graph[(rows, batch)] = _lib.launches - before

@@ -31,9 +31,11 @@ class PagedAttention(nn.Module):
         self.lam_q = None                       # [H_q, D] expanded over each GQA group
 
     def set_smooth_lambda(self, lam: torch.Tensor):
-        self.lam = lam
+        """``lam [H_kv, D]`` from the calibration file, kept in fp16 (the dtype the
+        reference multiplies in, attention.py:76-77)."""
+        self.lam = lam.to(torch.float16).contiguous()
         rep = self.num_heads // self.num_kv_heads
-        self.lam_q = lam.repeat_interleave(rep, dim=0).contiguous()
+        self.lam_q = self.lam.repeat_interleave(rep, dim=0).contiguous()
 
     def _prefill(self, ctx, q, k, v):
         out = torch.empty_like(q)
@@ -61,6 +63,19 @@ class PagedAttention(nn.Module):
                 vv.transpose(0, 1).unsqueeze(0), attn_mask=mask, scale=self.scale, enable_gqa=True)
             out[q0:q1] = o.squeeze(0).transpose(0, 1)
         return out
+
+    def attend(self, q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor):
+        """Attention for inputs that the fused pre-attention kernel has already
+        rotated, scaled and written to the pool: paged decode / verify, or
+        prefill over the step's fp16 rows plus the restored prefix."""
+        ctx = get_context()
+        if ctx.is_prefill:
+            return self._prefill(ctx, q.view(-1, self.num_heads, self.head_dim),
+                                 k.view(-1, self.num_kv_heads, self.head_dim),
+                                 v.view(-1, self.num_kv_heads, self.head_dim))
+        return paged_attention_decode(q, self.k_cache, self.v_cache, ctx.block_tables, ctx.context_lens,
+                                      block_n=self.block_n, num_kv_heads=self.num_kv_heads,
+                                      k_scale=self.k_cache[1], v_group=self.v_group, verify_m=ctx.verify_m)
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
         ctx = get_context()

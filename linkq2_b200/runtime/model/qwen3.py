@@ -13,10 +13,11 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 import torch
-import torch.nn.functional as F
 from torch import nn
 
+from linkq2_b200.kernels.fused import pre_attention, silu_mul
 from linkq2_b200.runtime.model.attention import PagedAttention
+from linkq2_b200.runtime.model.context import get_context
 from linkq2_b200.runtime.model.primitives import Linear, LMHead, RMSNorm, VocabEmbedding
 from linkq2_b200.runtime.model.rotary import RotaryEmbedding
 from linkq2_b200.runtime.parallel import get_tp
@@ -80,9 +81,16 @@ class Qwen3Attention(nn.Module):
         q = self.q_proj(hidden_states).view(-1, self.num_heads, self.head_dim)
         k = self.k_proj(hidden_states).view(-1, self.num_kv_heads, self.head_dim)
         v = self.v_proj(hidden_states).view(-1, self.num_kv_heads, self.head_dim)
-        q, k = self.q_norm(q), self.k_norm(k)
-        q, k = self.rotary_emb(positions, q, k)
-        o = self.attn(q, k, v)
+        # q/k norm, RoPE, SmoothAttention scaling and the KV4 store in one launch
+        ctx = get_context()
+        attn = self.attn
+        store = attn.k_cache is not None and ctx.slot_mapping is not None
+        q, k = pre_attention(q, k, v, self.q_norm.weight, self.k_norm.weight, self.rotary_emb.cos_sin_cache,
+                             positions, self.q_norm.eps, lam_q=attn.lam_q, lam_k=attn.lam,
+                             k_cache=attn.k_cache if store else None, v_cache=attn.v_cache if store else None,
+                             slot_mapping=ctx.slot_mapping if store else None, v_group=attn.v_group,
+                             want_k=ctx.is_prefill)
+        o = attn.attend(q, k, v)
         return self.tp.all_reduce(self.o_proj(o.flatten(1, -1)))
 
 
@@ -97,7 +105,7 @@ class Qwen3MLP(nn.Module):
         self.down_proj = Linear(inter, config.hidden_size)
 
     def forward(self, x):
-        return self.tp.all_reduce(self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x)))
+        return self.tp.all_reduce(self.down_proj(silu_mul(self.gate_proj(x), self.up_proj(x))))
 
 
 class Qwen3DecoderLayer(nn.Module):

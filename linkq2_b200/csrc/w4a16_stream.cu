@@ -7,28 +7,32 @@
 //   packed [K/8, N] int32 (n fastest; nibble j of word (k8, n) is k = 8*k8 + j),
 //   scales / zeros [K/group, N] fp16.
 //
-// Data movement.  A CTA of WN warps owns 32*WN output columns and a contiguous
-// range of K.  Packed words, scales, zero points and activations are copied
-// global -> shared with cp.async through a ring of STAGES buffers of 128 k each,
-// so the bytes in flight per SM are set by the ring depth, not by registers.
-// Lane (g, t) = (lane / 4, lane % 4) of a warp then reads one 128-bit word quad
-// per 32-k step, packed[k8 = 4*step + t][n0 .. n0+3] with n0 = 32*warp + 4*g; the
-// row pitch of the ring is padded by 32 bytes so these reads are conflict-free.
-// Nibbles are unpacked in registers and fed to the warp-level tensor-core op
-// m16n8k16 used as a dot-product engine: the MMA's 16 "rows" are output columns
-// (two per lane group), its 16 k-slots are the eight nibbles of lane t's words
-// in an order chosen so that unpacking needs one shift per word (the activation
-// fragment is permuted to match with four byte-permutes), and its 8 "columns"
-// are activation rows.  The four lanes of a group hold different k, so the MMA
-// performs the cross-lane reduction itself.
+// Data movement.  A CTA owns 32*WN output columns and a contiguous range of K.
+// One producer warp keeps a ring of STAGES shared-memory buffers (128 k each)
+// full with tiled TMA loads (cp.async.bulk.tensor, 128-byte swizzle, no
+// multicast) of packed words, activations, scales and zero points, signalled
+// through mbarriers; WN consumer warps wait on a stage, use it and hand it back.
+// Rows or columns past the end of a tensor are zero-filled by the TMA unit.  The
+// bytes in flight per SM are set by the ring depth, and the main loop has no
+// CTA-wide barrier.  Consumer lane (g, t) = (lane / 4, lane % 4) reads one
+// 128-bit word quad per step, packed[k8 row of (step, t)][n0 .. n0+3] with
+// n0 = 32*warp + 4*g, at its swizzled position; the rows a step uses are chosen
+// so that these reads are free of bank conflicts.
 //
-// For M <= 8 the group scale is applied after the group's integer dot product:
-//   y += s * (sum_k (u - 8) x_k  -  (z - 8) * sum_k x_k)
-// with the activation sum produced by one extra MMA against a fragment of ones.
-// For 8 < M <= 64 weights are dequantised to fp16 exactly as the reference does,
-// (u - z) * s rounded once (triton_kernels/utils.py:66-71; zero points must be
-// integer valued, which every reference quantizer guarantees), and accumulated
-// in fp32.
+// Arithmetic.  The nibbles go to the warp-level tensor-core op m16n8k16, used as
+// an fp32-accumulating dot-product engine, without any conversion: a nibble u
+// masked in place is the fp16 subnormal u * 2^-24 (even nibbles) or 16u * 2^-24
+// (odd nibbles, whose activations are divided by 16 to compensate), which the
+// tensor core multiplies exactly.  The MMA's 16 "rows" are output columns (two
+// per lane group), its 16 k-slots the eight nibbles of lane t's words in the
+// order the masks produce (the activation fragment is permuted to match), its 8
+// "columns" activation rows.  The four lanes of a group hold different k, so the
+// MMA performs the cross-lane reduction itself.  Per quantization group
+//   y += s * (2^24 * sum_k u' x_k  -  z * sum_k x_k),
+// the activation sum coming from one extra MMA against a constant fragment.
+// This equals sum_k ((u - z) * s) x_k of the reference's dequantisation
+// (triton_kernels/utils.py:66-71) evaluated in fp32, for any fp16 zero point;
+// the only rounding beyond fp32 accumulation is x/16 for |x| < 2^-10.
 //
 // Split-K.  The CTAs that share a column tile form a thread-block cluster along
 // grid.y.  Each leaves its fp32 partial tile in its own shared memory; after a
@@ -36,6 +40,11 @@
 // distributed shared memory, in rank order (so the result does not depend on
 // timing), and writes fp16.  No global scratch, no atomics.
 #include <cooperative_groups.h>
+#include <cuda.h>
+#ifdef LQ2_TUNING
+#include <cstdio>
+#include <cstdlib>
+#endif
 
 #include "common.cuh"
 
@@ -46,7 +55,6 @@ namespace lq2 {
 namespace {
 
 constexpr int kStageK = 128;                     // k per pipeline stage
-constexpr int kXsRowBytes = kStageK * 2 + 64;    // +64: conflict-free 128-bit fragment loads
 
 struct W4Params {
     const __half* x;
@@ -59,19 +67,45 @@ struct W4Params {
     int stages_per_rank;
 };
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
-    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    const int bytes = pred ? 16 : 0;             // 0 source bytes: the 16 destination bytes are zero-filled
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(bytes));
+// ---- mbarrier / bulk-copy primitives (shared::cta addresses as 32-bit values)
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Number of waits that gave up (see mbar_wait); stays 0 in a healthy run.
+__device__ unsigned int g_lq2_w4_wait_timeouts = 0;
+// Bounded wait: try_wait suspends the thread for a hardware time slice per call;
+// after kMaxWaitPolls unsuccessful polls the wait is abandoned, the give-up is
+// counted in g_lq2_w4_wait_timeouts and the kernel runs on to its end (its
+// output is then wrong, but the GPU is not left spinning).
+constexpr int kMaxWaitPolls = 1 << 22;
+__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity) {
+    for (int i = 0; i < kMaxWaitPolls; ++i)
+        if (mbar_try_wait(bar, parity)) return;
+    atomicAdd(&g_lq2_w4_wait_timeouts, 1u);
+}
+// 2-D tiled TMA load (no multicast): box at element coordinates (c0 = innermost, c1) -> shared memory
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
+        ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(bar) : "memory");
+}
 
-__device__ __forceinline__ uint32_t bcast_half(uint2 v, int idx) {
-    const uint32_t w = idx < 2 ? v.x : v.y;
-    return __byte_perm(w, w, (idx & 1) ? 0x3232 : 0x1010);
-}
 __device__ __forceinline__ float half_at(uint2 v, int idx) {
     const uint32_t w = idx < 2 ? v.x : v.y;
     return __half2float(__ushort_as_half((unsigned short)((idx & 1) ? (w >> 16) : (w & 0xffff))));
@@ -81,25 +115,46 @@ template <int NJ, int WN, int GPS>
 struct Layout {
     static constexpr int MT = 8 * NJ;
     static constexpr int TN = 32 * WN;
-    static constexpr int WROW = TN * 4 + 32;                 // bytes per packed row in the ring
-    static constexpr int W_BYTES = 16 * WROW;
-    static constexpr int X_BYTES = MT * kXsRowBytes;
+    static constexpr int KS = 1;                                // consumer warps that share a slab, splitting a stage's k
+    static constexpr int CONSUMERS = WN * KS;
+    static constexpr int THREADS = 32 * (CONSUMERS + 1);
+    static constexpr int SLAB_BYTES = 16 * 128;                 // one warp's 16 rows x 32 columns, 128B-swizzled
+    static constexpr int W_BYTES = WN * SLAB_BYTES;
+    static constexpr int XBOX_BYTES = MT * 128;                 // MT rows x 64 k, 128B-swizzled
+    static constexpr int X_BYTES = 2 * XBOX_BYTES;
     static constexpr int S_BYTES = GPS * TN * 2;
-    static constexpr int STAGE_BYTES = W_BYTES + X_BYTES + 2 * S_BYTES;
-    static constexpr int STAGES = NJ == 1 ? 6 : (NJ == 2 ? 6 : (NJ == 4 ? 5 : 4));
-    static constexpr int RED_BYTES = MT * TN * 4;
+    static constexpr int TX_BYTES = W_BYTES + X_BYTES;          // + S_BYTES (x2 with zero points)
+    static constexpr int STAGE_BYTES = (W_BYTES + X_BYTES + 2 * S_BYTES + 1023) / 1024 * 1024;
+#ifdef LQ2_STAGES
+    static constexpr int STAGES = LQ2_STAGES;
+#else
+    static constexpr int STAGES = NJ <= 2 ? 4 : 3;
+#endif
+    static constexpr int RED_BYTES = KS * MT * TN * 4;
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-    static constexpr int SMEM_BYTES = RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES;
+    static constexpr int DATA_BYTES = RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES;
+    static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + 2 * STAGES * 8;   // alignment slack + mbarriers
 };
 
+// Warps 0..CONSUMERS-1 consume (warp w works on column slab w % WN and on the
+// (w / WN)-th part of every stage's k range); the last warp is the producer that
+// keeps the ring full with TMA loads.  No CTA-wide barrier inside the main loop.
 template <int NJ, bool ZTABLE, int GPS, int WN>
-__global__ void __launch_bounds__(32 * WN, (NJ <= 2 ? 4 : 2)) w4a16_stream_kernel(const W4Params p) {
+__global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (NJ == 4 ? 2 : 1))) w4a16_stream_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                    const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
+                    const W4Params p) {
     using L = Layout<NJ, WN, GPS>;
-    constexpr bool SCALE_AFTER = (NJ == 1);
-    constexpr int MT = L::MT, TN = L::TN, THREADS = 32 * WN, STAGES = L::STAGES;
+    constexpr int MT = L::MT, TN = L::TN, STAGES = L::STAGES, KS = L::KS, CONSUMERS = L::CONSUMERS;
     constexpr int STEPS_PER_GROUP = 4 / GPS;
+    constexpr int STEPS = 4 / KS;                            // 32-k steps of a stage done by one consumer warp
+    // k8 row (and activation chunk) that lane t uses in step kk.  Rows 2t + (kk & 1) of an
+    // 8-row block make the swizzled 128-bit reads conflict-free; with four groups per
+    // stage a step must stay inside 4 consecutive rows instead.
+    constexpr bool INTERLEAVE = GPS <= 2;
 
-    extern __shared__ __align__(128) unsigned char smem[];
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // swizzle atoms are 1 KiB
+    const uint32_t bars = smem_u32(smem + L::DATA_BYTES);    // full[STAGES], empty[STAGES]
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -107,184 +162,139 @@ __global__ void __launch_bounds__(32 * WN, (NJ <= 2 ? 4 : 2)) w4a16_stream_kerne
     const int m0 = blockIdx.z * MT;
     const int rows = min(MT, p.m - m0);
     const int tile_n0 = blockIdx.x * TN;
-    const int nb = tile_n0 + warp * 32;
-    const bool n_ok = nb < p.n;
-    const int n0 = nb + 4 * g;
-    const int k8_total = p.k >> 3;
     const int total_stages = (p.k + kStageK - 1) / kStageK;
     const int ranks = gridDim.y, rank = blockIdx.y;
     const int s0 = min(total_stages, rank * p.stages_per_rank);
     const int s1 = min(total_stages, s0 + p.stages_per_rank);
     const int my_stages = s1 - s0;
-    const int groups_total = p.k / p.group;
 
-    auto issue = [&](int s, int buf) {
-        unsigned char* base = smem + buf * L::STAGE_BYTES;
-        // packed words: 16 rows x TN columns, 16-byte chunks
-        constexpr int WCHUNKS = 16 * (TN / 4);
-#pragma unroll
-        for (int c = tid; c < WCHUNKS; c += THREADS) {
-            const int row = c / (TN / 4), col4 = c % (TN / 4);
-            const int k8 = s * 16 + row, nn = tile_n0 + col4 * 4;
-            const bool ok = k8 < k8_total && nn < p.n;
-            cp_async16(base + row * L::WROW + col4 * 16, ok ? (const void*)(p.packed + int64_t(k8) * p.n + nn) : (const void*)p.packed, ok);
+    if (tid == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(bars + 8 * i, 1);                       // full: the producer's arrive + bytes
+            mbar_init(bars + 8 * (STAGES + i), CONSUMERS);    // empty: one arrive per consumer warp
         }
-        // activations: MT rows x 128 k, raw order
-        unsigned char* xb = base + L::W_BYTES;
-        constexpr int XCHUNKS = MT * 16;
-#pragma unroll
-        for (int c = tid; c < XCHUNKS; c += THREADS) {
-            const int row = c >> 4, kc = c & 15;
-            const int kk = s * kStageK + kc * 8;
-            const bool ok = row < rows && kk < p.k;
-            cp_async16(xb + row * kXsRowBytes + kc * 16, ok ? (const void*)(p.x + int64_t(m0 + row) * p.ldx + kk) : (const void*)p.x, ok);
-        }
-        // scales / zero points of the stage's groups: GPS rows x TN halves
-        unsigned char* sb = xb + L::X_BYTES;
-        constexpr int SCHUNKS = GPS * (TN / 8);
-        for (int c = tid; c < SCHUNKS; c += THREADS) {
-            const int q = c / (TN / 8), col8 = c % (TN / 8);
-            int gi = (GPS == 1) ? (s * kStageK) / p.group : s * GPS + q;
-            gi = min(gi, groups_total - 1);
-            const int nn = tile_n0 + col8 * 8;
-            const bool ok = nn < p.n;
-            cp_async16(sb + q * TN * 2 + col8 * 16, ok ? (const void*)(p.scales + int64_t(gi) * p.n + nn) : (const void*)p.scales, ok);
-            if (ZTABLE)
-                cp_async16(sb + L::S_BYTES + q * TN * 2 + col8 * 16, ok ? (const void*)(p.zeros + int64_t(gi) * p.n + nn) : (const void*)p.scales, ok);
-        }
-    };
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncthreads();
 
     float acc[2][NJ][4];
-    float gacc[2][SCALE_AFTER ? NJ : 1][4];
-    float xsum[SCALE_AFTER ? NJ : 1][4];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
         for (int j = 0; j < NJ; ++j)
 #pragma unroll
             for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) gacc[i][0][c] = 0.f;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) xsum[0][c] = 0.f;
 
-    const __half2 k1032 = __floats2half2_rn(1032.f, 1032.f);
-    const __half2 k16th = __floats2half2_rn(0.0625f, 0.0625f);
-    const __half2 km72 = __floats2half2_rn(-72.f, -72.f);
-    const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
-    const __half2 k64 = __floats2half2_rn(64.f, 64.f);
-    constexpr uint32_t kOnes = 0x3C003C00u;
-
+    const int slab = warp % WN, kpart = warp / WN;           // kpart == KS marks the producer
+    if (warp == CONSUMERS) {
+        // ------------------------------------------------------------ producer
+        for (int it = 0; it < my_stages; ++it) {
+            const int slot = it % STAGES, s = s0 + it;
+            if (it >= STAGES) mbar_wait(bars + 8 * (STAGES + slot), ((it / STAGES) - 1) & 1);
+            const uint32_t full = bars + 8 * slot;
+            const uint32_t base = smem_u32(smem + slot * L::STAGE_BYTES);
+            if (lane == 0) {
+                // Out-of-range rows and columns are zero-filled by the TMA unit and still
+                // count their full box size, so the expected byte count is a constant.
+                mbar_arrive_expect_tx(full, L::TX_BYTES + L::S_BYTES * (ZTABLE ? 2 : 1));
 #pragma unroll
-    for (int i = 0; i < STAGES - 1; ++i) {
-        if (i < my_stages) issue(s0 + i, i);
-        cp_async_commit();
-    }
-
-    for (int it = 0; it < my_stages; ++it) {
-        cp_async_wait<STAGES - 2>();
-        __syncthreads();
-        {
-            const int nxt = it + STAGES - 1;
-            if (nxt < my_stages) issue(s0 + nxt, nxt % STAGES);
-            cp_async_commit();
+                for (int w = 0; w < WN; ++w)
+                    tma_load_2d(base + w * L::SLAB_BYTES, &map_w, tile_n0 + 32 * w, s * 16, full);
+                tma_load_2d(base + L::W_BYTES, &map_x, s * kStageK, m0, full);
+                tma_load_2d(base + L::W_BYTES + L::XBOX_BYTES, &map_x, s * kStageK + 64, m0, full);
+                const int gi = (GPS == 1) ? (s * kStageK) / p.group : s * GPS;
+                tma_load_2d(base + L::W_BYTES + L::X_BYTES, &map_s, tile_n0, gi, full);
+                if (ZTABLE) tma_load_2d(base + L::W_BYTES + L::X_BYTES + L::S_BYTES, &map_z, tile_n0, gi, full);
+            }
+            __syncwarp();
         }
-        const unsigned char* base = smem + (it % STAGES) * L::STAGE_BYTES;
-        const unsigned char* wsm = base + warp * 128 + g * 16;
-        const unsigned char* xsm = base + L::W_BYTES;
-        const unsigned char* ssm = xsm + L::X_BYTES + warp * 64 + g * 8;
+    } else {
+        // ------------------------------------------------------------ consumers
+        float gacc[2][NJ][4];
+        float xsum[NJ][4];
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            const uint4 wq = *reinterpret_cast<const uint4*>(wsm + (kk * 4 + t) * L::WROW);
-            const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
-            uint4 xb[NJ];
+        for (int j = 0; j < NJ; ++j) {
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) {
-                const uint4 r = *reinterpret_cast<const uint4*>(xsm + (8 * j + g) * kXsRowBytes + (kk * 4 + t) * 16);
-                // halves x0..x7 -> {x0,x4} {x1,x5} {x2,x6} {x3,x7}: the k-slot order of the A fragments
-                xb[j].x = __byte_perm(r.x, r.z, 0x5410);
-                xb[j].y = __byte_perm(r.x, r.z, 0x7632);
-                xb[j].z = __byte_perm(r.y, r.w, 0x5410);
-                xb[j].w = __byte_perm(r.y, r.w, 0x7632);
+            for (int c = 0; c < 4; ++c) {
+                gacc[0][j][c] = 0.f;
+                gacc[1][j][c] = 0.f;
+                xsum[j][c] = 0.f;
             }
-            const int gq = kk / STEPS_PER_GROUP;
-            uint2 sc = make_uint2(0, 0), zc = make_uint2(0, 0);
-            if (!SCALE_AFTER || (kk + 1) % STEPS_PER_GROUP == 0) {
-                sc = *reinterpret_cast<const uint2*>(ssm + gq * TN * 2);
-                if (ZTABLE) zc = *reinterpret_cast<const uint2*>(ssm + L::S_BYTES + gq * TN * 2);
-            }
+        }
+        const __half2 k16th = __floats2half2_rn(0.0625f, 0.0625f);
+        constexpr uint32_t kOnes = 0x3C003C00u;
+        constexpr float kTwo24 = 16777216.f;
+        for (int it = 0; it < my_stages; ++it) {
+            const int slot = it % STAGES;
+            mbar_wait(bars + 8 * slot, (it / STAGES) & 1);
+            const unsigned char* base = smem + slot * L::STAGE_BYTES;
+            const unsigned char* wsm = base + slab * L::SLAB_BYTES;
+            const unsigned char* xsm = base + L::W_BYTES;
+            const unsigned char* ssm = xsm + L::X_BYTES + slab * 64 + g * 8;
+#ifdef LQ2_SKIP_COMPUTE
+            if (p.m < 0)
+#endif
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                __half2 s_a, s_b, zlo_a, zlo_b, zhi_a, zhi_b;
-                if (!SCALE_AFTER) {
-                    s_a = u32_as_h2(bcast_half(sc, 2 * i));
-                    s_b = u32_as_h2(bcast_half(sc, 2 * i + 1));
-                    if (ZTABLE) {
-                        const __half2 z_a = u32_as_h2(bcast_half(zc, 2 * i));
-                        const __half2 z_b = u32_as_h2(bcast_half(zc, 2 * i + 1));
-                        zlo_a = __hadd2(z_a, k1024);
-                        zlo_b = __hadd2(z_b, k1024);
-                        zhi_a = __hneg2(__hadd2(z_a, k64));
-                        zhi_b = __hneg2(__hadd2(z_b, k64));
-                    } else {
-                        zlo_a = zlo_b = k1032;
-                        zhi_a = zhi_b = km72;
-                    }
+            for (int ks = 0; ks < STEPS; ++ks) {
+                const int kk = kpart * STEPS + ks;
+                const int row = INTERLEAVE ? 8 * (kk >> 1) + 2 * t + (kk & 1) : 4 * kk + t;
+                // 128B swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
+                const uint4 wq = *reinterpret_cast<const uint4*>(wsm + row * 128 + ((g ^ (row & 7)) << 4));
+                const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
+                uint4 xb[NJ];
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) {
+                    const uint4 r = *reinterpret_cast<const uint4*>(
+                        xsm + (row >> 3) * L::XBOX_BYTES + (8 * j + g) * 128 + (((row & 7) ^ g) << 4));
+                    // halves x0..x7 -> {x0,x4} {x1,x5}/16 {x2,x6} {x3,x7}/16: the k-slot order of the A
+                    // fragments; odd nibbles enter A multiplied by 16 (no shift), so their x is divided by 16
+                    xb[j].x = __byte_perm(r.x, r.z, 0x5410);
+                    xb[j].y = h2_as_u32(__hmul2(u32_as_h2(__byte_perm(r.x, r.z, 0x7632)), k16th));
+                    xb[j].z = __byte_perm(r.y, r.w, 0x5410);
+                    xb[j].w = h2_as_u32(__hmul2(u32_as_h2(__byte_perm(r.y, r.w, 0x7632)), k16th));
                 }
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint32_t wa = wv[2 * i] >> (8 * h);
-                    const uint32_t wb = wv[2 * i + 1] >> (8 * h);
-                    const __half2 lo_a = u32_as_h2(and_or(wa, 0x000f000fu, 0x64006400u));
-                    const __half2 hi_a = u32_as_h2(and_or(wa, 0x00f000f0u, 0x64006400u));
-                    const __half2 lo_b = u32_as_h2(and_or(wb, 0x000f000fu, 0x64006400u));
-                    const __half2 hi_b = u32_as_h2(and_or(wb, 0x00f000f0u, 0x64006400u));
-                    uint32_t a0, a1, a2, a3;
-                    if (SCALE_AFTER) {
-                        a0 = h2_as_u32(__hsub2(lo_a, k1032));
-                        a1 = h2_as_u32(__hsub2(lo_b, k1032));
-                        a2 = h2_as_u32(__hfma2(hi_a, k16th, km72));
-                        a3 = h2_as_u32(__hfma2(hi_b, k16th, km72));
-                    } else {
-                        a0 = h2_as_u32(__hmul2(__hsub2(lo_a, zlo_a), s_a));
-                        a1 = h2_as_u32(__hmul2(__hsub2(lo_b, zlo_b), s_b));
-                        a2 = h2_as_u32(__hmul2(__hfma2(hi_a, k16th, zhi_a), s_a));
-                        a3 = h2_as_u32(__hmul2(__hfma2(hi_b, k16th, zhi_b), s_b));
-                    }
+                for (int i = 0; i < 2; ++i) {
 #pragma unroll
-                    for (int j = 0; j < NJ; ++j) {
-                        const uint32_t b0 = h ? xb[j].z : xb[j].x;
-                        const uint32_t b1 = h ? xb[j].w : xb[j].y;
-                        if constexpr (SCALE_AFTER) mma_m16n8k16(gacc[i][j], a0, a1, a2, a3, b0, b1);
-                        else mma_m16n8k16(acc[i][j], a0, a1, a2, a3, b0, b1);
+                    for (int h = 0; h < 2; ++h) {
+                        // nibbles as fp16 subnormals: u * 2^-24 (even nibbles) and 16u * 2^-24 (odd nibbles)
+                        const uint32_t wa = wv[2 * i] >> (8 * h);
+                        const uint32_t wb = wv[2 * i + 1] >> (8 * h);
+                        const uint32_t a0 = wa & 0x000f000fu, a1 = wb & 0x000f000fu;
+                        const uint32_t a2 = wa & 0x00f000f0u, a3 = wb & 0x00f000f0u;
+#pragma unroll
+                        for (int j = 0; j < NJ; ++j)
+                            mma_m16n8k16(gacc[i][j], a0, a1, a2, a3, h ? xb[j].z : xb[j].x, h ? xb[j].w : xb[j].y);
                     }
                 }
-            }
-            if constexpr (SCALE_AFTER) {
-                if (ZTABLE) {
+#ifndef LQ2_NO_XSUM
 #pragma unroll
-                    for (int j = 0; j < NJ; ++j) {
-                        mma_m16n8k16(xsum[j], kOnes, kOnes, kOnes, kOnes, xb[j].x, xb[j].y);
-                        mma_m16n8k16(xsum[j], kOnes, kOnes, kOnes, kOnes, xb[j].z, xb[j].w);
-                    }
+                for (int j = 0; j < NJ; ++j) {
+                    // sum of the step's activations (undoing the 1/16 on the odd slots with 16.0 in A)
+                    constexpr uint32_t k16s = 0x4C004C00u;
+                    mma_m16n8k16(xsum[j], kOnes, kOnes, k16s, k16s, xb[j].x, xb[j].y);
+                    mma_m16n8k16(xsum[j], kOnes, kOnes, k16s, k16s, xb[j].z, xb[j].w);
                 }
-                if ((kk + 1) % STEPS_PER_GROUP == 0) {
+#endif
+                // end of a scale group, or of this warp's share of one (the scale then multiplies a
+                // partial sum, which is the same by linearity)
+                if ((ks + 1) % (STEPS_PER_GROUP < STEPS ? STEPS_PER_GROUP : STEPS) == 0) {
+                    const int gq = kk / STEPS_PER_GROUP;
+                    const uint2 sc = *reinterpret_cast<const uint2*>(ssm + gq * TN * 2);
+                    uint2 zc = make_uint2(0x48004800u, 0x48004800u);           // 8.0 x4
+                    if (ZTABLE) zc = *reinterpret_cast<const uint2*>(ssm + L::S_BYTES + gq * TN * 2);
 #pragma unroll
                     for (int i = 0; i < 2; ++i) {
+                        // s * sum_k (u - z) x = (s * 2^24) * gacc - (s * z) * xsum
                         const float sa = half_at(sc, 2 * i), sb = half_at(sc, 2 * i + 1);
-                        float za = 0.f, zb = 0.f;
-                        if (ZTABLE) {
-                            za = half_at(zc, 2 * i) - 8.f;
-                            zb = half_at(zc, 2 * i + 1) - 8.f;
-                        }
+                        const float za = -sa * half_at(zc, 2 * i), zb = -sb * half_at(zc, 2 * i + 1);
+                        const float ta = sa * kTwo24, tb = sb * kTwo24;
 #pragma unroll
                         for (int j = 0; j < NJ; ++j) {
-                            acc[i][j][0] += sa * (gacc[i][j][0] - za * xsum[j][0]);
-                            acc[i][j][1] += sa * (gacc[i][j][1] - za * xsum[j][1]);
-                            acc[i][j][2] += sb * (gacc[i][j][2] - zb * xsum[j][0]);
-                            acc[i][j][3] += sb * (gacc[i][j][3] - zb * xsum[j][1]);
+                            acc[i][j][0] = fmaf(ta, gacc[i][j][0], fmaf(za, xsum[j][0], acc[i][j][0]));
+                            acc[i][j][1] = fmaf(ta, gacc[i][j][1], fmaf(za, xsum[j][1], acc[i][j][1]));
+                            acc[i][j][2] = fmaf(tb, gacc[i][j][2], fmaf(zb, xsum[j][0], acc[i][j][2]));
+                            acc[i][j][3] = fmaf(tb, gacc[i][j][3], fmaf(zb, xsum[j][1], acc[i][j][3]));
 #pragma unroll
                             for (int c = 0; c < 4; ++c) gacc[i][j][c] = 0.f;
                         }
@@ -295,12 +305,17 @@ __global__ void __launch_bounds__(32 * WN, (NJ <= 2 ? 4 : 2)) w4a16_stream_kerne
                         for (int c = 0; c < 4; ++c) xsum[j][c] = 0.f;
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bars + 8 * (STAGES + slot));
         }
     }
-    cp_async_wait<0>();
 
-    // ---- write-out.  Lane (g, t) owns columns n0..n0+3 of rows m0 + 8j + 2t (+1).
-    if (ranks == 1) {
+    const int nb = tile_n0 + slab * 32;
+    const bool n_ok = warp < CONSUMERS && nb < p.n;
+    const int n0 = nb + 4 * g;
+
+    // ---- write-out.  Consumer lane (g, t) owns columns n0..n0+3 of rows m0 + 8j + 2t (+1).
+    if (ranks == 1 && KS == 1) {
         if (n_ok) {
 #pragma unroll
             for (int j = 0; j < NJ; ++j) {
@@ -322,29 +337,34 @@ __global__ void __launch_bounds__(32 * WN, (NJ <= 2 ? 4 : 2)) w4a16_stream_kerne
     // ---- cluster reduction through distributed shared memory
     cg::cluster_group cluster = cg::this_cluster();
     __syncthreads();                                   // every warp is done with the ring
-    float* red = reinterpret_cast<float*>(smem);       // [MT][TN]
+    float* red = reinterpret_cast<float*>(smem);       // [KS][MT][TN]
+    if (warp < CONSUMERS) {
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) {
+        for (int j = 0; j < NJ; ++j) {
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int ml = 8 * j + 2 * t + r;
-            *reinterpret_cast<float4*>(red + ml * TN + warp * 32 + 4 * g) =
-                make_float4(acc[0][j][r], acc[0][j][2 + r], acc[1][j][r], acc[1][j][2 + r]);
+            for (int r = 0; r < 2; ++r) {
+                const int ml = 8 * j + 2 * t + r;
+                *reinterpret_cast<float4*>(red + (kpart * MT + ml) * TN + slab * 32 + 4 * g) =
+                    make_float4(acc[0][j][r], acc[0][j][2 + r], acc[1][j][r], acc[1][j][2 + r]);
+            }
         }
     }
     cluster.sync();
     {
-        const int slice = TN / ranks;                  // columns this rank finishes (ranks <= 8 divides TN)
-        const int c0 = rank * slice;
-        const int quads = slice / 4;
-        for (int e = tid; e < rows * quads; e += THREADS) {
-            const int ml = e / quads, cq = e % quads;
-            const int col = c0 + cq * 4;
+        // rank r finishes column quads [q0, q1) of the tile
+        constexpr int QUADS = TN / 4;
+        const int q0 = rank * QUADS / ranks, q1 = (rank + 1) * QUADS / ranks;
+        const int quads = q1 - q0;
+        for (int e = tid; e < rows * quads; e += L::THREADS) {
+            const int ml = e / quads, col = (q0 + e % quads) * 4;
             float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int q = 0; q < ranks; ++q) {
                 const float* remote = cluster.map_shared_rank(red, q);
-                const float4 v = *reinterpret_cast<const float4*>(remote + ml * TN + col);
-                sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+#pragma unroll
+                for (int kp = 0; kp < KS; ++kp) {
+                    const float4 v = *reinterpret_cast<const float4*>(remote + (kp * MT + ml) * TN + col);
+                    sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+                }
             }
             const int nn = tile_n0 + col;
             if (nn < p.n) {
@@ -361,21 +381,63 @@ struct Plan {
     int nj, wn, m_tiles, n_tiles, ranks, spr;
 };
 
+// Column-tile width and cluster size from shapes only.  Streaming is fastest when
+// every CTA is resident at once (up to four per SM) and each one streams a long
+// K range, so: 128-column tiles unless even the largest cluster leaves SMs
+// without a CTA, and the largest power-of-two cluster (K split) that keeps the
+// grid within one resident wave and gives every rank at least two stages.
 Plan make_plan(int m, int n, int k) {
-    Plan p;
-    p.nj = m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8));
-    p.m_tiles = cdiv(m, 8 * p.nj);
+    const int nj = m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8));
+    const int m_tiles = cdiv(m, 8 * nj);
     const int stages = cdiv(k, kStageK);
-    const int target = 2 * kNumSMs;
-    // 128-column tiles when that alone (times the largest cluster) fills the machine, else 64
-    p.wn = (cdiv(n, 128) * p.m_tiles * 8 >= target) ? 4 : 2;
-    p.n_tiles = cdiv(n, 32 * p.wn);
-    const int base = p.n_tiles * p.m_tiles;
-    int ranks = 1;
-    while (ranks < 8 && base * ranks < target && stages / (ranks * 2) >= 2) ranks *= 2;
-    p.spr = cdiv(stages, ranks);
-    p.ranks = ranks;
-    return p;
+    const int resident = kNumSMs * (nj <= 2 ? 4 : (nj == 4 ? 2 : 1));
+    const int wn = cdiv(n, 128) * m_tiles * 8 >= kNumSMs ? 4 : 2;
+    const int n_tiles = cdiv(n, 32 * wn);
+    const int base = n_tiles * m_tiles;
+    int r = 1;
+    while (r < 8 && base * r * 2 <= resident && stages / (r * 2) >= 2) r *= 2;
+    Plan best{nj, wn, m_tiles, n_tiles, r, cdiv(stages, r)};
+#ifdef LQ2_TUNING
+    if (const char* e = getenv("LQ2_W4_PLAN")) {      // "wn,ranks" override for sweeps
+        int wn = 0, r = 0;
+        if (sscanf(e, "%d,%d", &wn, &r) == 2 && (wn == 2 || wn == 4) && r >= 1 && r <= 8 && r <= stages)
+            best = Plan{nj, wn, m_tiles, cdiv(n, 32 * wn), r, cdiv(stages, r)};
+    }
+#endif
+    return best;
+}
+
+// ---- tensor maps.  cuTensorMapEncodeTiled is a driver entry point; it is looked up
+// through the runtime so that the library does not link against libcuda.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult res;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &res) != cudaSuccess ||
+            res != cudaDriverEntryPointSuccess)
+            ptr = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    return fn;
+}
+
+// rows x cols row-major matrix of elem_bytes elements with row pitch pitch_bytes; box = box_cols x box_rows
+bool make_map(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const void* base, uint64_t cols,
+              uint64_t rows, uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {pitch_bytes};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    (void)elem_bytes;
+    return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int NJ, bool ZTABLE, int GPS, int WN>
@@ -390,9 +452,18 @@ int launch_one(const W4Params& p, const Plan& pl, cudaStream_t st) {
             return LQ2_ERR_CUDA;
         configured[dev] = true;
     }
+    alignas(64) CUtensorMap map_w, map_x, map_s, map_z;
+    const uint64_t n = uint64_t(p.n), k = uint64_t(p.k), groups = uint64_t(p.k / p.group);
+    bool ok = make_map(&map_w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, p.packed, n, k / 8, n * 4, 32, 16, true);
+    ok = ok && make_map(&map_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.x, k, uint64_t(p.m), uint64_t(p.ldx) * 2, 64,
+                        L::MT, true);
+    ok = ok && make_map(&map_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.scales, n, groups, n * 2, L::TN, GPS, false);
+    ok = ok && make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ZTABLE ? p.zeros : p.scales, n, groups, n * 2,
+                        L::TN, GPS, false);
+    if (!ok) return LQ2_ERR_CUDA;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(pl.n_tiles, pl.ranks, pl.m_tiles);
-    cfg.blockDim = dim3(32 * WN);
+    cfg.blockDim = dim3(L::THREADS);
     cfg.dynamicSmemBytes = L::SMEM_BYTES;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -402,7 +473,7 @@ int launch_one(const W4Params& p, const Plan& pl, cudaStream_t st) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? LQ2_OK : LQ2_ERR_CUDA;
+    return cudaLaunchKernelEx(&cfg, kernel, map_w, map_x, map_s, map_z, p) == cudaSuccess ? LQ2_OK : LQ2_ERR_CUDA;
 }
 
 template <int NJ, bool ZTABLE, int GPS>

@@ -46,6 +46,34 @@ class B200Linear(QuantLinear):
         layer._meta = (4, group_size, 15, 8, _FP16, _FP16, _FP32, _FP16, 0, 3, True, 104)
         return layer
 
+    @classmethod
+    @torch.no_grad()
+    def fuse_columns(cls, layers):
+        """One layer computing ``cat([l(x) for l in layers], -1)``: the packed
+        words, scales and zero points of projections that share their input are
+        concatenated along N, which the ``[K/8, N]`` layout allows without
+        repacking.  Only for layers without an AWQ ``input_scale`` (each AWQ module
+        divides its input by its own vector, ``gemlite.py:41-42``) and with equal
+        K, group size and zero mode."""
+        first = layers[0]
+        for l in layers:
+            if l.input_scale is not None:
+                raise ValueError("projections with an input_scale cannot be fused")
+            if (l.in_features, l.group_size, l.zeros.numel() == 1) != \
+                    (first.in_features, first.group_size, first.zeros.numel() == 1):
+                raise ValueError("projections differ in K, group size or zero mode")
+        fused = cls()
+        fused.in_features = first.in_features
+        fused.out_features = sum(l.out_features for l in layers)
+        fused.group_size, fused.compute_dtype = first.group_size, first.compute_dtype
+        fused.register_buffer("packed", torch.cat([l.packed for l in layers], dim=1).contiguous())
+        fused.register_buffer("scales", torch.cat([l.scales for l in layers], dim=1).contiguous())
+        fused.register_buffer("zeros", first.zeros.clone() if first.zeros.numel() == 1
+                              else torch.cat([l.zeros for l in layers], dim=1).contiguous())
+        fused.register_buffer("input_scale", None)
+        fused._meta = first._meta
+        return fused
+
     def forward(self, x):
         if x.dtype != self.compute_dtype:
             raise TypeError(f"expected {self.compute_dtype}, got {x.dtype}")

@@ -58,6 +58,16 @@ class ModelConfig:
                    tie_word_embeddings=True)
 
 
+def _fuse(layers):
+    """Fused W4 projection for layers sharing their input, or None when they are
+    not packed W4 layers or carry AWQ input scales (the reason the reference keeps
+    them apart, ``qslab/runtime/model/qwen3.py:3-5``)."""
+    from linkq2_b200.runtime.backends.b200 import B200Linear
+    if not all(isinstance(l, B200Linear) and l.input_scale is None for l in layers):
+        return None
+    return B200Linear.fuse_columns(layers)
+
+
 class Qwen3Attention(nn.Module):
     def __init__(self, config: ModelConfig, rope: RotaryEmbedding):
         super().__init__()
@@ -72,15 +82,28 @@ class Qwen3Attention(nn.Module):
         self.k_proj = Linear(config.hidden_size, self.kv_size)
         self.v_proj = Linear(config.hidden_size, self.kv_size)
         self.o_proj = Linear(self.q_size, config.hidden_size)
+        self.qkv_proj = None
         self.rotary_emb = rope
         self.attn = PagedAttention(self.num_heads, self.head_dim, self.head_dim ** -0.5, self.num_kv_heads)
         self.q_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
         self.k_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
 
+    def fuse(self):
+        """Replace q/k/v by one projection when the checkpoint allows it."""
+        self.qkv_proj = _fuse([self.q_proj, self.k_proj, self.v_proj])
+        if self.qkv_proj is not None:
+            self.q_proj = self.k_proj = self.v_proj = None
+
     def forward(self, positions, hidden_states):
-        q = self.q_proj(hidden_states).view(-1, self.num_heads, self.head_dim)
-        k = self.k_proj(hidden_states).view(-1, self.num_kv_heads, self.head_dim)
-        v = self.v_proj(hidden_states).view(-1, self.num_kv_heads, self.head_dim)
+        if self.qkv_proj is not None:
+            q, k, v = self.qkv_proj(hidden_states).split([self.q_size, self.kv_size, self.kv_size], dim=-1)
+            q = q.unflatten(-1, (self.num_heads, self.head_dim))
+            k = k.unflatten(-1, (self.num_kv_heads, self.head_dim))
+            v = v.unflatten(-1, (self.num_kv_heads, self.head_dim))
+        else:
+            q = self.q_proj(hidden_states).view(-1, self.num_heads, self.head_dim)
+            k = self.k_proj(hidden_states).view(-1, self.num_kv_heads, self.head_dim)
+            v = self.v_proj(hidden_states).view(-1, self.num_kv_heads, self.head_dim)
         # q/k norm, RoPE, SmoothAttention scaling and the KV4 store in one launch
         ctx = get_context()
         attn = self.attn
@@ -103,9 +126,20 @@ class Qwen3MLP(nn.Module):
         self.gate_proj = Linear(config.hidden_size, inter)
         self.up_proj = Linear(config.hidden_size, inter)
         self.down_proj = Linear(inter, config.hidden_size)
+        self.gate_up_proj = None
+
+    def fuse(self):
+        """Replace gate/up by one projection when the checkpoint allows it."""
+        self.gate_up_proj = _fuse([self.gate_proj, self.up_proj])
+        if self.gate_up_proj is not None:
+            self.gate_proj = self.up_proj = None
 
     def forward(self, x):
-        return self.tp.all_reduce(self.down_proj(silu_mul(self.gate_proj(x), self.up_proj(x))))
+        if self.gate_up_proj is not None:
+            gate, up = self.gate_up_proj(x).chunk(2, dim=-1)
+        else:
+            gate, up = self.gate_proj(x), self.up_proj(x)
+        return self.tp.all_reduce(self.down_proj(silu_mul(gate, up)))
 
 
 class Qwen3DecoderLayer(nn.Module):
@@ -155,6 +189,15 @@ class Qwen3ForCausalLM(nn.Module):
         self.lm_head = LMHead(config.vocab_size, config.hidden_size)
         if config.tie_word_embeddings:
             self.lm_head.weight = self.model.embed_tokens.weight
+
+    def fuse_projections(self):
+        """Fuse q/k/v and gate/up of every layer into single W4 launches (a
+        load-time layout step: buffers are concatenated along N, nothing is
+        repacked).  Layers of AWQ checkpoints are left as they are."""
+        for layer in self.model.layers:
+            layer.self_attn.fuse()
+            layer.mlp.fuse()
+        return self
 
     def forward(self, input_ids, positions):
         return self.model(input_ids, positions)

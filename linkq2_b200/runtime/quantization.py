@@ -141,6 +141,8 @@ def build_from_checkpoint(path, *, device="cuda:0", max_position=None, fake=Fals
     with torch.device("meta"):
         model = Qwen3ForCausalLM(cfg, max_position, device=device)
     load_checkpoint_weights(model, path, device=device, fake=fake)
+    if not fake:
+        model.fuse_projections()
     return model.eval()
 
 
@@ -204,4 +206,5 @@ def build_random(cfg: ModelConfig, *, seed=0, group_size=128, device="cuda:0", m
     for name, param in list(model.named_parameters()):
         if param.is_meta:                      # the RMSNorm weights
             _set_param(model, name, torch.ones(param.shape, dtype=torch.float16, device=dev))
+    model.fuse_projections()
     return model.eval()

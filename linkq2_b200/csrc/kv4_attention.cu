@@ -57,6 +57,7 @@ struct AttnParams {
     __half* out;
     int batch, m, hq, hkv, page, max_blocks, ng, vg_shift;
     int num_blocks;
+    int page_shift;    // log2(page) when page is a power of two, else -1
     int splits;
     float sl2;  // D^-0.5 * log2(e)
     float* partial;
@@ -358,6 +359,436 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
     if (tid == 0) *counter = 0;
 }
 
+// =====================================================================================
+// Fast decode path: at most 8 query rows per KV head (one decode position of a GQA group
+// of up to 8 heads, or a few verify positions), D in {64, 128}, at most two V groups.
+//
+// One CTA of 8 warps serves (sequence, split, group of `hpc` KV heads); warp w works on
+// KV head w % hpc and on every (8/hpc)-th 32-token tile of the split.  Each warp keeps a
+// private ring of cp.async stages (K rows, V rows) in shared memory, so the bytes in
+// flight do not occupy registers and no CTA barrier is needed in the loop.
+//
+// Both products put the *cache* in the 16-row A operand of m16n8k16 and the (few) query
+// rows in the 8-column B operand, so nothing is padded from 4 rows to 16:
+//   S^T[token, row] = K[token, :] . Q'[row, :]     A = K nibbles, B = Q'^T
+//   O^T[dim, row]  += V^T[dim, token] . P'[token, row]   A = V nibbles, B = P'^T
+// Nibbles enter A as fp16 subnormals by masking alone (u * 2^-24, or 16u * 2^-24 for odd
+// nibbles); the offsets and scales are applied outside the MMAs:
+//   S  = 2^24 * acc - 8 * sum_d Q'[row, d]          (Q' = fp16(q * ks), /16 on odd slots)
+//   O  = 2^24 * acc - 8 * sum_t P'[t, row],  P'[t, row] = p[t, row] * vs[t, group]
+// P' is moved from the accumulator layout to the B layout with movmatrix.
+// =====================================================================================
+constexpr int kFastWarps = 8;
+constexpr int kFastThreads = kFastWarps * 32;
+constexpr int kFastTile = 32;                 // tokens per stage
+constexpr int kFastStages = 3;
+
+template <int D>
+struct FastLayout {
+    static constexpr int KROW = D / 2;                    // bytes per token row of one head
+    static constexpr int VROW = D / 2 + 16;               // padded: conflict-free 32-bit column reads
+    static constexpr int K_BYTES = kFastTile * KROW;
+    static constexpr int V_BYTES = kFastTile * VROW;
+    static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+    static constexpr int WARP_BYTES = kFastStages * STAGE_BYTES;
+    static constexpr int RING_BYTES = kFastWarps * WARP_BYTES;
+    static constexpr int MERGE_BYTES = kFastWarps * 8 * (D + 2) * 4;
+    static constexpr int SMEM_BYTES = RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES;
+};
+
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+// 2^x for x <= 0 (or -inf): the hardware approximation, 2 ulp
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(d) : "r"(a));
+    return d;
+}
+
+template <int D, int NG>
+__global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const AttnParams p, const int hpc) {
+    using L = FastLayout<D>;
+    constexpr int NW = D / 8;             // words per (token, head)
+    constexpr int KWT = NW / 4;           // K words per lane per token
+    constexpr int VW = NW / 8;            // V words per lane per token (word wsel*8 + g)
+    constexpr int NO = 4 * VW;            // O accumulators per lane (each 16 dims x 8 rows)
+    constexpr int KCH = D / 32;           // 16-byte chunks per lane per K (or V) tile
+
+    extern __shared__ __align__(16) unsigned char fsm[];
+    __shared__ int s_ticket;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int wt = kFastWarps / hpc;                       // warps that share a head
+    const int kvh = blockIdx.y * hpc + warp % hpc, ws = warp / hpc;
+    const int split = blockIdx.x, seq = blockIdx.z;
+    const int rep = p.hq / p.hkv;
+    const int rows_valid = p.m * rep;
+
+    const int capacity = p.max_blocks * p.page;
+    const int len = p.lens[seq];
+    const int reach = min(len + p.m - 1, capacity);
+    const int tiles = reach > 0 ? (reach + kFastTile - 1) / kFastTile : 0;
+    const int per_split = (tiles + p.splits - 1) / p.splits;
+    const int tile_begin = split * per_split;
+    const int tile_end = min(tiles, tile_begin + per_split);
+    const int first = tile_begin + ws;
+    const int n_my = first < tile_end ? (tile_end - first + wt - 1) / wt : 0;
+
+    // ---- Q'^T fragments (B operand): column n = g is query row g; lane t covers words 4t..4t+3
+    const bool row_ok = g < rows_valid;
+    uint32_t qb[KWT][2][2];
+    float qsum = 0.f;
+    {
+        const int mrow = row_ok ? g / rep : 0;
+        const __half* qp = p.q + int64_t(seq * p.m + mrow) * p.q_stride + (kvh * rep + (row_ok ? g % rep : 0)) * D;
+        const __half* ksp = p.ks + kvh * D;
+        const bool vec = (reinterpret_cast<uintptr_t>(qp) & 15) == 0;
+#pragma unroll
+        for (int wi = 0; wi < KWT; ++wi) {
+            const int d0 = 8 * (t * KWT + wi);
+            __half qraw[8], sraw[8];
+            *reinterpret_cast<uint4*>(sraw) = *reinterpret_cast<const uint4*>(ksp + d0);
+            if (vec) {
+                *reinterpret_cast<uint4*>(qraw) = *reinterpret_cast<const uint4*>(qp + d0);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) qraw[i] = qp[d0 + i];
+            }
+            __half qv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float v = row_ok ? __half2float(qraw[i]) * __half2float(sraw[i]) : 0.f;
+                // odd nibbles enter the A operand multiplied by 16
+                qv[i] = (i & 1) ? __float2half_rn(__half2float(__float2half_rn(v)) * 0.0625f) : __float2half_rn(v);
+                qsum += (i & 1) ? __half2float(qv[i]) * 16.f : __half2float(qv[i]);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                qb[wi][h][0] = h2_as_u32(__halves2half2(qv[2 * h], qv[2 * h + 4]));
+                qb[wi][h][1] = h2_as_u32(__halves2half2(qv[2 * h + 1], qv[2 * h + 5]));
+            }
+        }
+    }
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);                 // sum over all D for row g
+    const float c1 = 16777216.f * p.sl2;
+    // this lane's accumulator columns are rows 2t and 2t+1
+    const float cq0 = 8.f * p.sl2 * __shfl_sync(0xffffffffu, qsum, (2 * t) * 4);
+    const float cq1 = 8.f * p.sl2 * __shfl_sync(0xffffffffu, qsum, (2 * t + 1) * 4);
+    const int r0 = 2 * t, r1 = 2 * t + 1;
+    const int lim0 = r0 < rows_valid ? min(len + r0 / rep, capacity) : 0;
+    const int lim1 = r1 < rows_valid ? min(len + r1 / rep, capacity) : 0;
+    const int lim_min = rows_valid == 8 ? min(len, capacity) : 0;   // a padded (invalid) row is masked everywhere
+
+    float o[NO][4];
+#pragma unroll
+    for (int j = 0; j < NO; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[j][c] = 0.f;
+    float mx0 = -INFINITY, mx1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float lp[NG][2];
+#pragma unroll
+    for (int q = 0; q < NG; ++q) lp[q][0] = lp[q][1] = 0.f;
+
+    unsigned char* ring = fsm + warp * L::WARP_BYTES;
+    const int64_t head_words = int64_t(p.hkv) * NW;
+    uint32_t live_bits = 0;
+
+    // lane-constant parts of the copy addresses: chunk c = lane + 32 j of a tile is
+    // (token c / chunks_per_row, 16-byte part c % chunks_per_row)
+    int64_t src_off[KCH];
+    int kdst[KCH], vdst[KCH];
+#pragma unroll
+    for (int j = 0; j < KCH; ++j) {
+        const int c = lane + 32 * j;
+        const int tok = c / (L::KROW / 16), part = c % (L::KROW / 16);
+        src_off[j] = tok * head_words + kvh * NW + part * 4;
+        kdst[j] = tok * L::KROW + part * 16;
+        vdst[j] = L::K_BYTES + tok * L::VROW + part * 16;
+    }
+    const __half* vs_lane = p.vs + (int64_t(lane) * p.hkv + kvh) * NG;
+    const int32_t* bt_row = p.bt + int64_t(seq) * p.max_blocks;
+    const int tiles_per_page = p.page / kFastTile;
+    int cached_page = -1, cached_raw = -1;
+
+    uint32_t sc_ring[kFastStages];
+#pragma unroll
+    for (int i = 0; i < kFastStages; ++i) sc_ring[i] = 0;
+
+    auto issue = [&](int idx, int slot, uint32_t& sc) {
+        const int tile = first + idx * wt;
+        int page_idx, in_page;
+        if (p.page_shift >= 0) {
+            page_idx = (tile * kFastTile) >> p.page_shift;
+            in_page = (tile * kFastTile) & (p.page - 1);
+        } else {
+            page_idx = tile / tiles_per_page;
+            in_page = (tile - page_idx * tiles_per_page) * kFastTile;
+        }
+        if (page_idx != cached_page) {
+            cached_page = page_idx;
+            cached_raw = bt_row[page_idx];
+        }
+        const bool ok = cached_raw >= 0;
+        live_bits = (live_bits & ~(1u << slot)) | (uint32_t(ok) << slot);
+        if (!ok) return;
+        const int64_t slot0 = int64_t(min(cached_raw, p.num_blocks - 1)) * p.page + in_page;
+        unsigned char* dst = ring + slot * L::STAGE_BYTES;
+        const uint32_t* ksrc = p.kq + slot0 * head_words;
+        const uint32_t* vsrc = p.vq + slot0 * head_words;
+#pragma unroll
+        for (int j = 0; j < KCH; ++j) {
+            cp_async_16(dst + kdst[j], ksrc + src_off[j]);
+            cp_async_16(dst + vdst[j], vsrc + src_off[j]);
+        }
+        const __half* sp = vs_lane + slot0 * p.hkv * NG;
+        sc = NG == 2 ? *reinterpret_cast<const uint32_t*>(sp) : uint32_t(__half_as_ushort(sp[0]));
+    };
+
+#pragma unroll
+    for (int i = 0; i < kFastStages - 1; ++i) {
+        if (i < n_my) issue(i, i, sc_ring[i]);
+        cp_async_commit();
+    }
+
+    for (int it = 0; it < n_my; ++it) {
+        const int slot = it % kFastStages;
+        {
+            const int nxt = it + kFastStages - 1;
+            // the register ring of scales rotates with the stages: entry (nxt % stages)
+            uint32_t sc_new = 0;
+            if (nxt < n_my) issue(nxt, nxt % kFastStages, sc_new);
+            cp_async_commit();
+#pragma unroll
+            for (int i = 0; i < kFastStages; ++i)
+                if (i == nxt % kFastStages) sc_ring[i] = sc_new;
+        }
+        cp_async_wait<kFastStages - 1>();
+        __syncwarp();
+        uint32_t sc_cur = 0;
+#pragma unroll
+        for (int i = 0; i < kFastStages; ++i)
+            if (i == slot) sc_cur = sc_ring[i];
+        if ((live_bits >> slot) & 1u) {
+            const unsigned char* kb = ring + slot * L::STAGE_BYTES;
+            const unsigned char* vb = kb + L::K_BYTES;
+            const int pos0 = (first + it * wt) * kFastTile;
+            float sv[2][4];
+#pragma unroll
+            for (int b16 = 0; b16 < 2; ++b16) {
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                const int tokA = 16 * b16 + g, tokB = tokA + 8;
+                uint32_t ka[KWT], kbw[KWT];
+                if (KWT == 4) {
+                    const uint4 x = *reinterpret_cast<const uint4*>(kb + tokA * L::KROW + t * 16);
+                    const uint4 y = *reinterpret_cast<const uint4*>(kb + tokB * L::KROW + t * 16);
+                    ka[0] = x.x; ka[1] = x.y; ka[KWT - 2] = x.z; ka[KWT - 1] = x.w;
+                    kbw[0] = y.x; kbw[1] = y.y; kbw[KWT - 2] = y.z; kbw[KWT - 1] = y.w;
+                } else {
+                    const uint2 x = *reinterpret_cast<const uint2*>(kb + tokA * L::KROW + t * 8);
+                    const uint2 y = *reinterpret_cast<const uint2*>(kb + tokB * L::KROW + t * 8);
+                    ka[0] = x.x; ka[1] = x.y; kbw[0] = y.x; kbw[1] = y.y;
+                }
+#pragma unroll
+                for (int wi = 0; wi < KWT; ++wi) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t wa = ka[wi] >> (8 * h), wb = kbw[wi] >> (8 * h);
+                        mma_m16n8k16(acc, wa & 0x000f000fu, wb & 0x000f000fu, wa & 0x00f000f0u, wb & 0x00f000f0u,
+                                     qb[wi][h][0], qb[wi][h][1]);
+                    }
+                }
+                sv[b16][0] = fmaf(acc[0], c1, -cq0);
+                sv[b16][1] = fmaf(acc[1], c1, -cq1);
+                sv[b16][2] = fmaf(acc[2], c1, -cq0);
+                sv[b16][3] = fmaf(acc[3], c1, -cq1);
+                if (pos0 + kFastTile > lim_min) {            // warp-uniform: only the last tiles need masks
+                    const int pa = pos0 + tokA, pb = pos0 + tokB;
+                    if (pa >= lim0) sv[b16][0] = -INFINITY;
+                    if (pa >= lim1) sv[b16][1] = -INFINITY;
+                    if (pb >= lim0) sv[b16][2] = -INFINITY;
+                    if (pb >= lim1) sv[b16][3] = -INFINITY;
+                }
+            }
+            float t0 = fmaxf(fmaxf(sv[0][0], sv[0][2]), fmaxf(sv[1][0], sv[1][2]));
+            float t1 = fmaxf(fmaxf(sv[0][1], sv[0][3]), fmaxf(sv[1][1], sv[1][3]));
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+                t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+            }
+            const float n0 = fmaxf(mx0, t0), n1 = fmaxf(mx1, t1);
+            const float safe0 = n0 == -INFINITY ? 0.f : n0, safe1 = n1 == -INFINITY ? 0.f : n1;
+            const float a0 = ex2(mx0 - safe0), a1 = ex2(mx1 - safe1);
+            mx0 = n0; mx1 = n1;
+            if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
+                l0 *= a0; l1 *= a1;
+#pragma unroll
+                for (int q = 0; q < NG; ++q) { lp[q][0] *= a0; lp[q][1] *= a1; }
+#pragma unroll
+                for (int j = 0; j < NO; ++j) { o[j][0] *= a0; o[j][1] *= a1; o[j][2] *= a0; o[j][3] *= a1; }
+            }
+#pragma unroll
+            for (int b16 = 0; b16 < 2; ++b16) {
+                const float p0 = ex2(sv[b16][0] - safe0), p1 = ex2(sv[b16][1] - safe1);
+                const float p2 = ex2(sv[b16][2] - safe0), p3 = ex2(sv[b16][3] - safe1);
+                l0 += p0 + p2;
+                l1 += p1 + p3;
+                const uint32_t sA = __shfl_sync(0xffffffffu, sc_cur, 16 * b16 + g);
+                const uint32_t sB = __shfl_sync(0xffffffffu, sc_cur, 16 * b16 + g + 8);
+                const unsigned char* vrow = vb + (16 * b16) * L::VROW;
+#pragma unroll
+                for (int q = 0; q < NG; ++q) {
+                    const float fa = __half2float(__ushort_as_half((unsigned short)(q ? (sA >> 16) : (sA & 0xffff))));
+                    const float fb = __half2float(__ushort_as_half((unsigned short)(q ? (sB >> 16) : (sB & 0xffff))));
+                    const float e0 = p0 * fa, e1 = p1 * fa, e2 = p2 * fb, e3 = p3 * fb;
+                    lp[q][0] += e0 + e2;
+                    lp[q][1] += e1 + e3;
+                    const uint32_t b0 = movmatrix_trans(pack_h2(e0, e1));
+                    const uint32_t b1 = movmatrix_trans(pack_h2(e2, e3));
+#pragma unroll
+                    for (int wsel = (NG == 2 ? q : 0); wsel < (NG == 2 ? q + 1 : VW); ++wsel) {
+                        const int wo = (wsel * 8 + g) * 4;
+                        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(vrow + (2 * t) * L::VROW + wo);
+                        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(vrow + (2 * t + 1) * L::VROW + wo);
+                        const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vrow + (2 * t + 8) * L::VROW + wo);
+                        const uint32_t w3 = *reinterpret_cast<const uint32_t*>(vrow + (2 * t + 9) * L::VROW + wo);
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const uint32_t sel = b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12);
+                            const uint32_t xa = __byte_perm(w0, w1, sel), xb = __byte_perm(w2, w3, sel);
+                            mma_m16n8k16(o[wsel * 4 + b], xa & 0x000f000fu, xa & 0x00f000f0u, xb & 0x000f000fu,
+                                         xb & 0x00f000f0u, b0, b1);
+                        }
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    }
+    cp_async_wait<0>();
+
+    // ---- per-warp results: rows 2t, 2t+1 of 16 * VW * ... dims; denominators summed over the 8 lane groups
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+#pragma unroll
+        for (int q = 0; q < NG; ++q) {
+            lp[q][0] += __shfl_xor_sync(0xffffffffu, lp[q][0], off);
+            lp[q][1] += __shfl_xor_sync(0xffffffffu, lp[q][1], off);
+        }
+    }
+    __syncthreads();                                   // all rings are idle: reuse them for the merge
+    float* mo = reinterpret_cast<float*>(fsm) + warp * 8 * (D + 2);     // [8 rows][D + 2]
+#pragma unroll
+    for (int j = 0; j < NO; ++j) {
+        const int wsel = j / 4, b = j % 4;
+        const int grp = NG == 2 ? wsel : 0;
+        const int dim = 8 * (wsel * 8 + g) + 2 * b;
+        mo[r0 * (D + 2) + dim] = o[j][0] * 16777216.f - 8.f * lp[grp][0];
+        mo[r1 * (D + 2) + dim] = o[j][1] * 16777216.f - 8.f * lp[grp][1];
+        mo[r0 * (D + 2) + dim + 1] = o[j][2] * 1048576.f - 8.f * lp[grp][0];
+        mo[r1 * (D + 2) + dim + 1] = o[j][3] * 1048576.f - 8.f * lp[grp][1];
+    }
+    if (g == 0) {
+        mo[r0 * (D + 2) + D] = mx0; mo[r0 * (D + 2) + D + 1] = l0;
+        mo[r1 * (D + 2) + D] = mx1; mo[r1 * (D + 2) + D + 1] = l1;
+    }
+    __syncthreads();
+
+    // ---- merge the wt warps of each head, then write the result or this split's partial
+    const int splits = p.splits;
+    const float* all = reinterpret_cast<const float*>(fsm);
+    constexpr int D4 = D / 4;
+    for (int e = tid; e < hpc * rows_valid * D4; e += kFastThreads) {
+        const int d = (e % D4) * 4, hr = e / D4;
+        const int hl = hr / rows_valid, row = hr - hl * rows_valid;
+        const int head = blockIdx.y * hpc + hl;
+        float mx = -INFINITY;
+        for (int w = 0; w < wt; ++w) mx = fmaxf(mx, all[((w * hpc + hl) * 8 + row) * (D + 2) + D]);
+        const float safe = mx == -INFINITY ? 0.f : mx;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float den = 0.f;
+        for (int w = 0; w < wt; ++w) {
+            const float* src = all + ((w * hpc + hl) * 8 + row) * (D + 2);
+            const float f = ex2(src[D] - safe);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] += src[d + i] * f;
+            den += src[D + 1] * f;
+        }
+        if (splits == 1) {
+            const int mrow = row / rep, qh = head * rep + row % rep;
+            const float inv = 1.f / fmaxf(den, 1e-20f);
+            __half2 h01 = __floats2half2_rn(acc[0] * inv, acc[1] * inv), h23 = __floats2half2_rn(acc[2] * inv, acc[3] * inv);
+            *reinterpret_cast<uint2*>(p.out + (int64_t(seq * p.m + mrow) * p.hq + qh) * D + d) =
+                make_uint2(h2_as_u32(h01), h2_as_u32(h23));
+        } else {
+            float* dst = p.partial + ((int64_t(seq * p.hkv + head) * splits + split) * rows_valid + row) * (D + 2);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) __stcg(dst + d + i, acc[i]);
+            if (d == 0) { __stcg(dst + D, mx); __stcg(dst + D + 1, den); }
+        }
+    }
+    if (splits == 1) return;
+
+    __threadfence();
+    __syncthreads();
+    int* counter = p.counters + seq * gridDim.y + blockIdx.y;
+    if (tid == 0) s_ticket = atomicAdd(counter, 1);
+    __syncthreads();
+    if (s_ticket != splits - 1) return;
+    __threadfence();
+    for (int e = tid; e < hpc * rows_valid * D4; e += kFastThreads) {
+        const int d = (e % D4) * 4, hr = e / D4;
+        const int hl = hr / rows_valid, row = hr - hl * rows_valid;
+        const int head = blockIdx.y * hpc + hl;
+        const float* part = p.partial + (int64_t(seq * p.hkv + head) * splits) * rows_valid * (D + 2);
+        float mx = -INFINITY;
+        for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, __ldcg(part + (int64_t(sp) * rows_valid + row) * (D + 2) + D));
+        const float safe = mx == -INFINITY ? 0.f : mx;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float den = 0.f;
+        for (int sp = 0; sp < splits; ++sp) {
+            const float* src = part + (int64_t(sp) * rows_valid + row) * (D + 2);
+            const float f = ex2(__ldcg(src + D) - safe);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] += __ldcg(src + d + i) * f;
+            den += __ldcg(src + D + 1) * f;
+        }
+        const int mrow = row / rep, qh = head * rep + row % rep;
+        const float inv = 1.f / fmaxf(den, 1e-20f);
+        __half2 h01 = __floats2half2_rn(acc[0] * inv, acc[1] * inv), h23 = __floats2half2_rn(acc[2] * inv, acc[3] * inv);
+        *reinterpret_cast<uint2*>(p.out + (int64_t(seq * p.m + mrow) * p.hq + qh) * D + d) =
+            make_uint2(h2_as_u32(h01), h2_as_u32(h23));
+    }
+    if (tid == 0) *counter = 0;
+}
+
+// KV heads per CTA for the fast path: as many as possible (their rows are adjacent in
+// memory) while the grid can still fill the machine twice.
+int fast_heads_per_cta(int batch, int hkv, int64_t capacity) {
+    int hpc = 1;
+    while (hpc * 2 <= 8 && hkv % (hpc * 2) == 0) hpc *= 2;
+    const int64_t max_splits = capacity / 512 > 0 ? (capacity / 512 < 64 ? capacity / 512 : 64) : 1;
+    while (hpc > 1 && int64_t(batch) * (hkv / hpc) * max_splits < 2 * kNumSMs) hpc /= 2;
+    return hpc;
+}
+
+bool fast_path_ok(int m, int hq, int hkv, int d, int page, int ng) {
+    return m * (hq / hkv) <= 8 && page % kFastTile == 0 && (ng == 1 || (ng == 2 && d == 128));
+}
+
 constexpr int kMaxCounters = 1 << 16;
 
 int row_tiles(int m, int hq, int hkv) {
@@ -370,12 +801,14 @@ int row_tiles(int m, int hq, int hkv) {
 int kv4_attention_splits(int batch, int m, int hq, int hkv, int d, int page, int max_blocks) {
     (void)d; (void)m; (void)hq;
     const int64_t capacity = int64_t(max_blocks) * page;
-    const int base = batch * hkv;
-    // Enough CTAs to fill the machine three times over, and no CTA longer than
-    // 4096 tokens so that one long sequence in a batch cannot become the tail;
-    // never less than 256 tokens of capacity per split.
-    int64_t splits = cdiv(3 * kNumSMs, base);
-    const int64_t by_len = cdiv64(capacity, 4096);
+    // Shapes only.  A CTA covers hpc KV heads with 8 / hpc warps per head; enough splits
+    // to fill the machine twice, no warp longer than 1024 tokens (so one long sequence in
+    // a batch cannot become the tail), never less than 256 tokens of capacity per split.
+    const int hpc = fast_heads_per_cta(batch, hkv, capacity);
+    const int wt = 8 / hpc;
+    const int base = batch * (hkv / hpc);
+    int64_t splits = 2 * kNumSMs / base;                 // floor: the grid stays within one resident wave
+    const int64_t by_len = cdiv64(capacity, int64_t(1024) * wt);
     if (by_len > splits) splits = by_len;
     const int64_t most = capacity / 256 > 0 ? capacity / 256 : 1;
     if (splits > most) splits = most;
@@ -430,10 +863,31 @@ int kv4_attention_launch(const __half* q, int64_t q_stride, const uint32_t* kq, 
     while ((1 << shift) < v_group) ++shift;
     p.vg_shift = shift;
     p.num_blocks = int(num_slots / page);
+    p.page_shift = -1;
+    for (int sft = 0; sft < 31; ++sft)
+        if ((1 << sft) == page) p.page_shift = sft;
     p.splits = kv4_attention_splits(batch, m, hq, hkv, d, page, max_blocks);
     p.sl2 = float(1.4426950408889634 / sqrt(double(d)));
     p.counters = reinterpret_cast<int*>(workspace);
     p.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + size_t(kMaxCounters) * sizeof(int));
+    if (fast_path_ok(m, hq, hkv, d, page, p.ng)) {
+        const int hpc = fast_heads_per_cta(batch, hkv, int64_t(max_blocks) * page);
+        dim3 fgrid(p.splits, hkv / hpc, batch);
+        static bool configured[64] = {};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LQ2_ERR_CUDA;
+        if (!configured[dev]) {
+            bool ok = cudaFuncSetAttribute(kv4_decode_fast_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, FastLayout<128>::SMEM_BYTES) == cudaSuccess;
+            ok = ok && cudaFuncSetAttribute(kv4_decode_fast_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, FastLayout<128>::SMEM_BYTES) == cudaSuccess;
+            ok = ok && cudaFuncSetAttribute(kv4_decode_fast_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, FastLayout<64>::SMEM_BYTES) == cudaSuccess;
+            if (!ok) return LQ2_ERR_CUDA;
+            configured[dev] = true;
+        }
+        if (d == 128 && p.ng == 2) kv4_decode_fast_kernel<128, 2><<<fgrid, kFastThreads, FastLayout<128>::SMEM_BYTES, st>>>(p, hpc);
+        else if (d == 128) kv4_decode_fast_kernel<128, 1><<<fgrid, kFastThreads, FastLayout<128>::SMEM_BYTES, st>>>(p, hpc);
+        else kv4_decode_fast_kernel<64, 1><<<fgrid, kFastThreads, FastLayout<64>::SMEM_BYTES, st>>>(p, hpc);
+        return check_launch();
+    }
     const int rt = row_tiles(m, hq, hkv);
     dim3 grid(p.splits, hkv, batch);
 #define LQ2_ATTN(DD, RR) kv4_attention_kernel<DD, RR><<<grid, kThreads, 0, st>>>(p)

@@ -341,7 +341,7 @@ def run_b200(args):
         ms_lin = a.elapsed_time(b) / reps
     peaks, which = measured_peaks()
     achieved = alg_bytes / (ms_lin * 1e-3) / 1e9
-    roofline = {"bound": "hbm", "kernel": f"w4a16_stream_kernel (M={BATCH}, all {len(lins)} W4A16 launches of one decode step)",
+    roofline = {"bound": "hbm", "kernel": f"w4a16_umma_kernel (M={BATCH}, all {len(lins)} W4A16 launches of one decode step)",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "of": which, "traffic": None,
                 "bytes_per_launch": round(alg_bytes / len(lins)), "us_per_launch": round(ms_lin * 1e3 / len(lins), 2)}

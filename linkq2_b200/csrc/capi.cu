@@ -7,6 +7,8 @@ int w4_pack_launch(const int8_t*, int, int32_t*, int, int, cudaStream_t);
 size_t w4a16_stream_workspace_bytes(int, int, int);
 int w4a16_stream_launch(const __half*, int64_t, const int32_t*, const __half*, const __half*, __half*,
                         int, int, int, int, void*, size_t, cudaStream_t);
+int w4a16_umma_launch(const __half*, int64_t, const int32_t*, const __half*, const __half*, __half*, int, int,
+                      int, int, cudaStream_t);
 int kv4_store_launch(const __half*, const __half*, int64_t, int64_t, uint32_t*, const __half*, uint32_t*,
                      __half*, const int32_t*, int, int, int, int, int64_t, cudaStream_t);
 int kv4_materialize_launch(const uint32_t*, const __half*, const uint32_t*, const __half*, const int64_t*,
@@ -71,6 +73,11 @@ int lq2_w4a16_linear(const void* x, int64_t x_row_stride, const int32_t* packed,
     if (!aligned(x, 16) || x_row_stride % 8 || x_row_stride < k || !aligned(packed, 16) ||
         !aligned(scales, 16) || (zeros && !aligned(zeros, 16)) || !aligned(y, 8))
         return LQ2_ERR_ALIGN;
+    // up to 8 rows: the weight-streaming kernel; beyond that the tcgen05 kernel
+    if (m > 8)
+        return w4a16_umma_launch(static_cast<const __half*>(x), x_row_stride, packed,
+                                 static_cast<const __half*>(scales), static_cast<const __half*>(zeros),
+                                 static_cast<__half*>(y), m, n, k, group, static_cast<cudaStream_t>(stream));
     return w4a16_stream_launch(static_cast<const __half*>(x), x_row_stride, packed,
                                static_cast<const __half*>(scales), static_cast<const __half*>(zeros),
                                static_cast<__half*>(y), m, n, k, group, workspace, workspace_bytes,

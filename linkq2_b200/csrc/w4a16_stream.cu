@@ -115,8 +115,10 @@ template <int NJ, int WN, int GPS>
 struct Layout {
     static constexpr int MT = 8 * NJ;
     static constexpr int TN = 32 * WN;
-    static constexpr int KS = 1;                                // consumer warps that share a slab, splitting a stage's k
-    static constexpr int CONSUMERS = WN * KS;
+    static constexpr int KS = 1;                                // (one consumer warp per k range of a stage)
+    static constexpr int NJW = NJ < 2 ? NJ : 2;                 // 8-row activation blocks per consumer warp
+    static constexpr int JS = NJ / NJW;                         // consumer warps that share a slab, splitting the rows
+    static constexpr int CONSUMERS = WN * JS;
     static constexpr int THREADS = 32 * (CONSUMERS + 1);
     static constexpr int SLAB_BYTES = 16 * 128;                 // one warp's 16 rows x 32 columns, 128B-swizzled
     static constexpr int W_BYTES = WN * SLAB_BYTES;
@@ -130,21 +132,22 @@ struct Layout {
 #else
     static constexpr int STAGES = NJ <= 2 ? 4 : 3;
 #endif
-    static constexpr int RED_BYTES = KS * MT * TN * 4;
+    static constexpr int RED_BYTES = MT * TN * 4;
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
     static constexpr int DATA_BYTES = RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES;
     static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + 2 * STAGES * 8;   // alignment slack + mbarriers
 };
 
-// Warps 0..CONSUMERS-1 consume (warp w works on column slab w % WN and on the
-// (w / WN)-th part of every stage's k range); the last warp is the producer that
+// Warps 0..CONSUMERS-1 consume: warp w works on column slab w % WN and on the
+// activation rows of block (w / WN) * 16 .. +15 (two 8-row MMA column blocks), so a
+// 32-row batch keeps eight consumer warps busy; the last warp is the producer that
 // keeps the ring full with TMA loads.  No CTA-wide barrier inside the main loop.
 template <int NJ, bool ZTABLE, int GPS, int WN>
-__global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (NJ == 4 ? 2 : 1))) w4a16_stream_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+__global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (NJ == 4 ? 3 : 1))) w4a16_stream_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                     const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                     const W4Params p) {
     using L = Layout<NJ, WN, GPS>;
-    constexpr int MT = L::MT, TN = L::TN, STAGES = L::STAGES, KS = L::KS, CONSUMERS = L::CONSUMERS;
+    constexpr int MT = L::MT, TN = L::TN, STAGES = L::STAGES, KS = L::KS, CONSUMERS = L::CONSUMERS, NJW = L::NJW;
     constexpr int STEPS_PER_GROUP = 4 / GPS;
     constexpr int STEPS = 4 / KS;                            // 32-k steps of a stage done by one consumer warp
     // k8 row (and activation chunk) that lane t uses in step kk.  Rows 2t + (kk & 1) of an
@@ -177,15 +180,16 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
     }
     __syncthreads();
 
-    float acc[2][NJ][4];
+    float acc[2][NJW][4];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int j = 0; j < NJ; ++j)
+        for (int j = 0; j < NJW; ++j)
 #pragma unroll
             for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
 
-    const int slab = warp % WN, kpart = warp / WN;           // kpart == KS marks the producer
+    const int slab = warp % WN, jpart = warp / WN;           // first activation block of this warp: jpart * NJW
+    constexpr int kpart = 0;
     if (warp == CONSUMERS) {
         // ------------------------------------------------------------ producer
         for (int it = 0; it < my_stages; ++it) {
@@ -210,10 +214,10 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
         }
     } else {
         // ------------------------------------------------------------ consumers
-        float gacc[2][NJ][4];
-        float xsum[NJ][4];
+        float gacc[2][NJW][4];
+        float xsum[NJW][4];
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) {
+        for (int j = 0; j < NJW; ++j) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 gacc[0][j][c] = 0.f;
@@ -241,11 +245,11 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
                 // 128B swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
                 const uint4 wq = *reinterpret_cast<const uint4*>(wsm + row * 128 + ((g ^ (row & 7)) << 4));
                 const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
-                uint4 xb[NJ];
+                uint4 xb[NJW];
 #pragma unroll
-                for (int j = 0; j < NJ; ++j) {
+                for (int j = 0; j < NJW; ++j) {
                     const uint4 r = *reinterpret_cast<const uint4*>(
-                        xsm + (row >> 3) * L::XBOX_BYTES + (8 * j + g) * 128 + (((row & 7) ^ g) << 4));
+                        xsm + (row >> 3) * L::XBOX_BYTES + (8 * (jpart * NJW + j) + g) * 128 + (((row & 7) ^ g) << 4));
                     // halves x0..x7 -> {x0,x4} {x1,x5}/16 {x2,x6} {x3,x7}/16: the k-slot order of the A
                     // fragments; odd nibbles enter A multiplied by 16 (no shift), so their x is divided by 16
                     xb[j].x = __byte_perm(r.x, r.z, 0x5410);
@@ -263,13 +267,13 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
                         const uint32_t a0 = wa & 0x000f000fu, a1 = wb & 0x000f000fu;
                         const uint32_t a2 = wa & 0x00f000f0u, a3 = wb & 0x00f000f0u;
 #pragma unroll
-                        for (int j = 0; j < NJ; ++j)
+                        for (int j = 0; j < NJW; ++j)
                             mma_m16n8k16(gacc[i][j], a0, a1, a2, a3, h ? xb[j].z : xb[j].x, h ? xb[j].w : xb[j].y);
                     }
                 }
 #ifndef LQ2_NO_XSUM
 #pragma unroll
-                for (int j = 0; j < NJ; ++j) {
+                for (int j = 0; j < NJW; ++j) {
                     // sum of the step's activations (undoing the 1/16 on the odd slots with 16.0 in A)
                     constexpr uint32_t k16s = 0x4C004C00u;
                     mma_m16n8k16(xsum[j], kOnes, kOnes, k16s, k16s, xb[j].x, xb[j].y);
@@ -290,7 +294,7 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
                         const float za = -sa * half_at(zc, 2 * i), zb = -sb * half_at(zc, 2 * i + 1);
                         const float ta = sa * kTwo24, tb = sb * kTwo24;
 #pragma unroll
-                        for (int j = 0; j < NJ; ++j) {
+                        for (int j = 0; j < NJW; ++j) {
                             acc[i][j][0] = fmaf(ta, gacc[i][j][0], fmaf(za, xsum[j][0], acc[i][j][0]));
                             acc[i][j][1] = fmaf(ta, gacc[i][j][1], fmaf(za, xsum[j][1], acc[i][j][1]));
                             acc[i][j][2] = fmaf(tb, gacc[i][j][2], fmaf(zb, xsum[j][0], acc[i][j][2]));
@@ -300,7 +304,7 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
                         }
                     }
 #pragma unroll
-                    for (int j = 0; j < NJ; ++j)
+                    for (int j = 0; j < NJW; ++j)
 #pragma unroll
                         for (int c = 0; c < 4; ++c) xsum[j][c] = 0.f;
                 }
@@ -318,10 +322,10 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
     if (ranks == 1 && KS == 1) {
         if (n_ok) {
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) {
+            for (int j = 0; j < NJW; ++j) {
 #pragma unroll
                 for (int r = 0; r < 2; ++r) {
-                    const int m = m0 + 8 * j + 2 * t + r;
+                    const int m = m0 + 8 * (jpart * NJW + j) + 2 * t + r;
                     if (m < p.m) {
                         const __half2 lo = __floats2half2_rn(acc[0][j][r], acc[0][j][2 + r]);
                         const __half2 hi = __floats2half2_rn(acc[1][j][r], acc[1][j][2 + r]);
@@ -337,14 +341,14 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
     // ---- cluster reduction through distributed shared memory
     cg::cluster_group cluster = cg::this_cluster();
     __syncthreads();                                   // every warp is done with the ring
-    float* red = reinterpret_cast<float*>(smem);       // [KS][MT][TN]
+    float* red = reinterpret_cast<float*>(smem);       // [MT][TN]
     if (warp < CONSUMERS) {
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) {
+        for (int j = 0; j < NJW; ++j) {
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                const int ml = 8 * j + 2 * t + r;
-                *reinterpret_cast<float4*>(red + (kpart * MT + ml) * TN + slab * 32 + 4 * g) =
+                const int ml = 8 * (jpart * NJW + j) + 2 * t + r;
+                *reinterpret_cast<float4*>(red + ml * TN + slab * 32 + 4 * g) =
                     make_float4(acc[0][j][r], acc[0][j][2 + r], acc[1][j][r], acc[1][j][2 + r]);
             }
         }
@@ -360,11 +364,8 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
             float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int q = 0; q < ranks; ++q) {
                 const float* remote = cluster.map_shared_rank(red, q);
-#pragma unroll
-                for (int kp = 0; kp < KS; ++kp) {
-                    const float4 v = *reinterpret_cast<const float4*>(remote + (kp * MT + ml) * TN + col);
-                    sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-                }
+                const float4 v = *reinterpret_cast<const float4*>(remote + ml * TN + col);
+                sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
             }
             const int nn = tile_n0 + col;
             if (nn < p.n) {
@@ -390,7 +391,7 @@ Plan make_plan(int m, int n, int k) {
     const int nj = m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8));
     const int m_tiles = cdiv(m, 8 * nj);
     const int stages = cdiv(k, kStageK);
-    const int resident = kNumSMs * (nj <= 2 ? 4 : (nj == 4 ? 2 : 1));
+    const int resident = kNumSMs * (nj <= 2 ? 4 : (nj == 4 ? 3 : 1));
     const int wn = cdiv(n, 128) * m_tiles * 8 >= kNumSMs ? 4 : 2;
     const int n_tiles = cdiv(n, 32 * wn);
     const int base = n_tiles * m_tiles;

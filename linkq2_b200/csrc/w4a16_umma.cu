@@ -1,0 +1,473 @@
+// W4A16 linear for M > 8 (batched decode, verify, prefill): int4 weights are
+// dequantised into shared memory and multiplied on the 5th-generation tensor
+// cores (tcgen05.mma) with the accumulator in tensor memory.
+//
+// Replaces the split-K and large-M Triton routes of the reference
+// (qslab/kernels/gemlite/triton_kernels/gemm_splitK_A16fWnO16f_int32packing.py:199-412,
+//  gemm_A16fWnO16f_int32packing.py:174-373) behind the same buffers.
+//
+// Orientation.  The product is computed transposed, Y^T[n, m] = W[n, :] . X[m, :],
+// so that the 128 rows of the MMA are output channels and its N dimension
+// (16..256) is the batch: a 32-row decode batch wastes nothing.  Per CTA: 128
+// output channels x MB batch rows, K streamed in stages of 64.
+//
+// Warp roles (10 warps):
+//   warp 0      producer: tiled TMA loads of packed words [8 x 128] int32, the
+//               activation tile [MB x 64] fp16 (128-byte swizzle, K-major: already
+//               the MMA's B operand layout), scales and zero points of the stage
+//   warps 2-9   dequantise: thread (n, half) turns 4 packed words of channel n into
+//               4 x 8 fp16 values, (u - z) * s rounded once exactly as the reference
+//               (triton_kernels/utils.py:66-71; integer-valued zero points), and
+//               stores them as 16-byte chunks of the K-major, 128-byte-swizzled A
+//               tile; the nibble masks yield k in the order 0,4,1,5,2,6,3,7 inside
+//               a chunk, so the same threads permute the activation tile's chunks
+//               in place to match
+//   warp 1      issues tcgen05.mma (M=128, N=MB, K=16, fp32 accumulate in TMEM) and
+//               commits each stage to the mbarrier that frees its buffers
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator, then the same cluster
+//               split-K reduction through distributed shared memory as the
+//               streaming kernel, fp16 store
+// All waits are bounded (see mbar_wait_bounded).
+#include <cooperative_groups.h>
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace lq2 {
+
+namespace {
+
+constexpr int kUM = 128;          // output channels per CTA (MMA M)
+constexpr int kUK = 64;           // k per stage
+constexpr int kUThreads = 320;    // 10 warps
+constexpr int kDequantThreads = 256;
+
+struct UParams {
+    __half* y;
+    int m, n, k, group;
+    int stages_per_rank;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Number of waits that gave up; stays 0 in a healthy run.
+__device__ unsigned int g_lq2_umma_wait_timeouts = 0;
+constexpr int kMaxWaitPolls = 1 << 22;
+// Bounded wait: after kMaxWaitPolls unsuccessful polls the wait is abandoned and counted,
+// and the kernel runs on to its end (wrong output, but no spinning GPU).
+__device__ __forceinline__ void mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    for (int i = 0; i < kMaxWaitPolls; ++i)
+        if (mbar_try_wait(bar, parity)) return;
+    atomicAdd(&g_lq2_umma_wait_timeouts, 1u);
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
+        ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(bar) : "memory");
+}
+
+// ---- tcgen05 wrappers (cta_group::1)
+__device__ __forceinline__ void tmem_alloc(uint32_t smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_dst), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// arrive on an mbarrier once all MMAs issued so far by this thread have completed
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
+}
+// 16 consecutive accumulator columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 64 fp16 (128 B),
+// 8-row groups 1024 B apart.  Fields: start address >> 4 in bits [0,14), leading-dimension
+// byte offset >> 4 in [16,30) (unused by swizzled K-major layouts), stride-dimension byte
+// offset >> 4 in [32,46), descriptor version 1 in [46,48), layout type SWIZZLE_128B = 2 in [61,64).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulator (bit 4), fp16 A and B (formats 0),
+// both K-major, N >> 3 in bits [17,23), M >> 4 in bits [24,29).
+__host__ __device__ constexpr uint32_t umma_idesc(int mma_m, int mma_n) {
+    return (1u << 4) | (uint32_t(mma_n >> 3) << 17) | (uint32_t(mma_m >> 4) << 24);
+}
+
+// Two rings: a deep one for what TMA delivers (packed words, activations, scales: ~9 KB per
+// stage at MB = 32), which sets the bytes in flight, and a shallow one for the 16 KB
+// dequantised A tiles.
+template <int MB, int GPSU>
+struct ULayout {
+    static constexpr int A_BYTES = kUM * 128;                       // [128 n][64 k] fp16, swizzled
+    static constexpr int A_STAGES = 2;
+    static constexpr int X_BYTES = (MB * 128 + 1023) / 1024 * 1024; // [MB m][64 k] fp16, swizzled
+    static constexpr int RAW_BYTES = 8 * kUM * 4;                   // [8 k8][128 n] int32
+    static constexpr int S_BYTES = GPSU * kUM * 2;                  // [GPSU][128 n] fp16
+    static constexpr int RAW_OFF = X_BYTES, S_OFF = RAW_OFF + RAW_BYTES, Z_OFF = S_OFF + S_BYTES;
+    static constexpr int R_STAGE_BYTES = (Z_OFF + S_BYTES + 1023) / 1024 * 1024;   // x tile first: 1 KiB aligned
+    static constexpr int R_STAGES = MB <= 64 ? 4 : (MB <= 128 ? 4 : 3);
+    static constexpr int TX_BYTES = MB * 128 + RAW_BYTES;           // + S_BYTES (x2 with zero points)
+    static constexpr int A_RING_OFF = 0, R_RING_OFF = A_STAGES * A_BYTES;
+    static constexpr int RING_BYTES = R_RING_OFF + R_STAGES * R_STAGE_BYTES;
+    static constexpr int RED_BYTES = MB * kUM * 4;
+    static constexpr int DATA_BYTES = RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES;
+    static constexpr int NBARS = 2 * R_STAGES + 2 * A_STAGES + 1;
+    static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + NBARS * 8 + 16;
+    static constexpr int TMEM_COLS = MB < 32 ? 32 : MB;
+};
+
+template <int MB, bool ZTABLE, int GPSU>
+__global__ void __launch_bounds__(kUThreads, 1)
+w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                  const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
+                  const UParams p) {
+    using L = ULayout<MB, GPSU>;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    constexpr int RS = L::R_STAGES, AS = L::A_STAGES;
+    const uint32_t bars = smem_u32(smem + L::DATA_BYTES);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::DATA_BYTES + L::NBARS * 8);
+    auto raw_full = [&](int s) { return bars + 8 * s; };               // TMA bytes of raw stage s landed
+    auto raw_free = [&](int s) { return bars + 8 * (RS + s); };        // MMAs that read its activations are done
+    auto a_full = [&](int s) { return bars + 8 * (2 * RS + s); };      // A tile s written by all dequant warps
+    auto a_free = [&](int s) { return bars + 8 * (2 * RS + AS + s); }; // MMAs that read A tile s are done
+    const uint32_t acc_full = bars + 8 * (2 * RS + 2 * AS);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tile_n0 = blockIdx.x * kUM;
+    const int m0 = blockIdx.z * MB;
+    const int rows = min(MB, p.m - m0);
+    const int total_stages = (p.k + kUK - 1) / kUK;
+    const int ranks = gridDim.y, rank = blockIdx.y;
+    const int s0 = min(total_stages, rank * p.stages_per_rank);
+    const int s1 = min(total_stages, s0 + p.stages_per_rank);
+    const int my_stages = s1 - s0;
+
+    if (tid == 0) {
+        for (int i = 0; i < RS; ++i) {
+            mbar_init(raw_full(i), 1);
+            mbar_init(raw_free(i), 1);
+        }
+        for (int i = 0; i < AS; ++i) {
+            mbar_init(a_full(i), kDequantThreads / 32);
+            mbar_init(a_free(i), 1);
+        }
+        mbar_init(acc_full, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), L::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    unsigned char* a_ring = smem + L::A_RING_OFF;
+    unsigned char* r_ring = smem + L::R_RING_OFF;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        for (int it = 0; it < my_stages; ++it) {
+            const int slot = it % RS, s = s0 + it;
+            if (it >= RS) mbar_wait_bounded(raw_free(slot), ((it / RS) - 1) & 1);
+            if (lane == 0) {
+                const uint32_t base = smem_u32(r_ring + slot * L::R_STAGE_BYTES);
+                mbar_arrive_expect_tx(raw_full(slot), L::TX_BYTES + L::S_BYTES * (ZTABLE ? 2 : 1));
+                tma_load_2d(base + L::RAW_OFF, &map_w, tile_n0, s * 8, raw_full(slot));
+                tma_load_2d(base, &map_x, s * kUK, m0, raw_full(slot));
+                const int gi = (GPSU == 1) ? (s * kUK) / p.group : s * GPSU;
+                tma_load_2d(base + L::S_OFF, &map_s, tile_n0, gi, raw_full(slot));
+                if (ZTABLE) tma_load_2d(base + L::Z_OFF, &map_z, tile_n0, gi, raw_full(slot));
+            }
+            __syncwarp();
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        constexpr uint32_t idesc = umma_idesc(kUM, MB);
+        for (int it = 0; it < my_stages; ++it) {
+            const int rslot = it % RS, aslot = it % AS;
+            mbar_wait_bounded(a_full(aslot), (it / AS) & 1);
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t abase = smem_u32(a_ring + aslot * L::A_BYTES);
+                const uint32_t xbase = smem_u32(r_ring + rslot * L::R_STAGE_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < kUK / 16; ++kk) {
+                    // a K step of 16 fp16 advances 32 bytes inside the 128-byte swizzled rows
+                    umma_f16(tmem_base, smem_desc_sw128(abase + kk * 32), smem_desc_sw128(xbase + kk * 32), idesc,
+                             (it > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(a_free(aslot));                   // both buffers are reusable once these MMAs are done
+                umma_commit(raw_free(rslot));
+                if (it == my_stages - 1) umma_commit(acc_full);
+            }
+            __syncwarp();
+        }
+    } else {
+        // ------------------------------------------------------------ dequantise
+        const int d = tid - 64;
+        const int nl = d & (kUM - 1), half = d >> 7;          // channel within the tile, k8 rows 4*half..+3
+        const __half2 k16th = __floats2half2_rn(0.0625f, 0.0625f);
+        const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
+        const __half2 k64 = __floats2half2_rn(64.f, 64.f);
+        for (int it = 0; it < my_stages; ++it) {
+            const int rslot = it % RS, aslot = it % AS;
+            unsigned char* rbase = r_ring + rslot * L::R_STAGE_BYTES;
+            mbar_wait_bounded(raw_full(rslot), (it / RS) & 1);
+            if (it >= AS) mbar_wait_bounded(a_free(aslot), ((it / AS) - 1) & 1);
+            // ---- activation tile: k order inside every 16-byte chunk -> 0,4,1,5,2,6,3,7
+            for (int c = d; c < MB * 8; c += kDequantThreads) {
+                uint4* ptr = reinterpret_cast<uint4*>(rbase + c * 16);
+                const uint4 r = *ptr;
+                uint4 o;
+                o.x = __byte_perm(r.x, r.z, 0x5410);
+                o.y = __byte_perm(r.x, r.z, 0x7632);
+                o.z = __byte_perm(r.y, r.w, 0x5410);
+                o.w = __byte_perm(r.y, r.w, 0x7632);
+                *ptr = o;
+            }
+            // ---- weights
+            const uint32_t* raw = reinterpret_cast<const uint32_t*>(rbase + L::RAW_OFF);
+            const __half* sc = reinterpret_cast<const __half*>(rbase + L::S_OFF);
+            const __half* zc = reinterpret_cast<const __half*>(rbase + L::Z_OFF);
+            unsigned char* arow = a_ring + aslot * L::A_BYTES + (nl >> 3) * 1024 + (nl & 7) * 128;
+            __half2 s2, zlo, zhi;
+            auto load_meta = [&](int gq) {
+                s2 = __half2half2(sc[gq * kUM + nl]);
+                const __half2 z2 = ZTABLE ? __half2half2(zc[gq * kUM + nl]) : __floats2half2_rn(8.f, 8.f);
+                zlo = __hadd2(z2, k1024);
+                zhi = __hneg2(__hadd2(z2, k64));
+            };
+            if (GPSU == 1) load_meta(0);
+#pragma unroll
+            for (int r4 = 0; r4 < 4; ++r4) {
+                const int r = 4 * half + r4;                  // k8 row inside the stage: k = 8r .. 8r+7
+                if (GPSU == 2 && r4 == 0) load_meta(half);    // two groups of 32 per stage: rows 0-3, 4-7
+                const uint32_t w = raw[r * kUM + nl];
+                const uint32_t w8 = w >> 8;
+                uint4 o;
+                o.x = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w, 0x000f000fu, 0x64006400u)), zlo), s2));
+                o.y = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
+                o.z = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w8, 0x000f000fu, 0x64006400u)), zlo), s2));
+                o.w = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w8, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
+                *reinterpret_cast<uint4*>(arow + ((r ^ (nl & 7)) << 4)) = o;
+            }
+            // generic-proxy stores must be visible to the tensor core's (async proxy) reads
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(a_full(aslot));
+        }
+    }
+
+    // ---- epilogue: warps 2-5 read the accumulator (TMEM lane = output channel)
+    cg::cluster_group cluster = cg::this_cluster();
+    float* red = reinterpret_cast<float*>(smem);          // [MB][128]
+    if (warp >= 2 && warp < 6) {
+        if (my_stages > 0) {
+            mbar_wait_bounded(acc_full, 0);
+            tc_fence_after();
+        }
+    }
+    __syncthreads();                                       // the ring is idle from here on
+    if (warp >= 2 && warp < 6) {
+        const int quarter = warp & 3;                      // TMEM lanes 32*quarter .. +31 belong to this warp
+        const int nl = quarter * 32 + lane;
+#pragma unroll
+        for (int c0 = 0; c0 < MB; c0 += 16) {
+            float v[16];
+            if (my_stages > 0) {
+                tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + c0, v);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) red[(c0 + i) * kUM + nl] = v[i];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem_base, L::TMEM_COLS);
+    if (ranks > 1) cluster.sync();
+    {
+        constexpr int QUADS = kUM / 4;
+        const int q0 = rank * QUADS / ranks, q1 = (rank + 1) * QUADS / ranks;
+        const int quads = q1 - q0;
+        for (int e = tid; e < rows * quads; e += kUThreads) {
+            const int ml = e / quads, col = (q0 + e % quads) * 4;
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q = 0; q < ranks; ++q) {
+                const float* src = ranks > 1 ? cluster.map_shared_rank(red, q) : red;
+                const float4 v = *reinterpret_cast<const float4*>(src + ml * kUM + col);
+                sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+            }
+            const int nn = tile_n0 + col;
+            if (nn < p.n) {
+                const __half2 lo = __floats2half2_rn(sum.x, sum.y);
+                const __half2 hi = __floats2half2_rn(sum.z, sum.w);
+                *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * p.n + nn) = make_uint2(h2_as_u32(lo), h2_as_u32(hi));
+            }
+        }
+    }
+    if (ranks > 1) cluster.sync();
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult res;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &res) != cudaSuccess ||
+            res != cudaDriverEntryPointSuccess)
+            ptr = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    return fn;
+}
+
+bool make_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t cols, uint64_t rows,
+              uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {pitch_bytes};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct UPlan {
+    int mb, m_tiles, n_tiles, ranks, spr;
+};
+
+// Batch tile and cluster size from shapes only: the largest power-of-two K split that
+// keeps the grid within one CTA per SM and leaves every rank at least four stages.
+UPlan make_uplan(int m, int n, int k) {
+    UPlan p;
+    p.mb = m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : (m <= 128 ? 128 : 256)));
+    p.m_tiles = cdiv(m, p.mb);
+    p.n_tiles = cdiv(n, kUM);
+    const int stages = cdiv(k, kUK);
+    const int base = p.n_tiles * p.m_tiles;
+    int r = 1;
+    while (r < 8 && base * r * 2 <= kNumSMs * (p.mb <= 32 ? 3 : (p.mb <= 64 ? 2 : 1)) && stages / (r * 2) >= 4) r *= 2;
+    p.ranks = r;
+    p.spr = cdiv(stages, r);
+    return p;
+}
+
+template <int MB, bool ZTABLE, int GPSU>
+int launch_umma(const __half* x, int64_t ldx, const int32_t* packed, const __half* scales, const __half* zeros,
+                const UParams& p, const UPlan& pl, cudaStream_t st) {
+    using L = ULayout<MB, GPSU>;
+    auto kernel = w4a16_umma_kernel<MB, ZTABLE, GPSU>;
+    static bool configured[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LQ2_ERR_CUDA;
+    if (!configured[dev]) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES) != cudaSuccess)
+            return LQ2_ERR_CUDA;
+        configured[dev] = true;
+    }
+    alignas(64) CUtensorMap map_w, map_x, map_s, map_z;
+    const uint64_t n = uint64_t(p.n), k = uint64_t(p.k), groups = uint64_t(p.k / p.group);
+    bool ok = make_map(&map_w, CU_TENSOR_MAP_DATA_TYPE_INT32, packed, n, k / 8, n * 4, kUM, 8, false);
+    ok = ok && make_map(&map_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, uint64_t(p.m), uint64_t(ldx) * 2, 64, MB, true);
+    ok = ok && make_map(&map_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales, n, groups, n * 2, kUM, GPSU, false);
+    ok = ok && make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ZTABLE ? zeros : scales, n, groups, n * 2, kUM, GPSU, false);
+    if (!ok) return LQ2_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.n_tiles, pl.ranks, pl.m_tiles);
+    cfg.blockDim = dim3(kUThreads);
+    cfg.dynamicSmemBytes = L::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = pl.ranks;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, map_w, map_x, map_s, map_z, p) == cudaSuccess ? LQ2_OK : LQ2_ERR_CUDA;
+}
+
+template <int MB, bool ZTABLE>
+int launch_umma_g(const __half* x, int64_t ldx, const int32_t* packed, const __half* scales, const __half* zeros,
+                  const UParams& p, const UPlan& pl, cudaStream_t st) {
+    if (p.group >= 64) return launch_umma<MB, ZTABLE, 1>(x, ldx, packed, scales, zeros, p, pl, st);
+    return launch_umma<MB, ZTABLE, 2>(x, ldx, packed, scales, zeros, p, pl, st);
+}
+
+template <int MB>
+int launch_umma_z(const __half* x, int64_t ldx, const int32_t* packed, const __half* scales, const __half* zeros,
+                  const UParams& p, const UPlan& pl, cudaStream_t st) {
+    return zeros ? launch_umma_g<MB, true>(x, ldx, packed, scales, zeros, p, pl, st)
+                 : launch_umma_g<MB, false>(x, ldx, packed, scales, zeros, p, pl, st);
+}
+
+}  // namespace
+
+int w4a16_umma_launch(const __half* x, int64_t ldx, const int32_t* packed, const __half* scales,
+                      const __half* zeros, __half* y, int m, int n, int k, int group, cudaStream_t st) {
+    const UPlan pl = make_uplan(m, n, k);
+    if (pl.m_tiles > 65535) return LQ2_ERR_SHAPE;
+    UParams p;
+    p.y = y; p.m = m; p.n = n; p.k = k; p.group = group; p.stages_per_rank = pl.spr;
+    switch (pl.mb) {
+        case 16: return launch_umma_z<16>(x, ldx, packed, scales, zeros, p, pl, st);
+        case 32: return launch_umma_z<32>(x, ldx, packed, scales, zeros, p, pl, st);
+        case 64: return launch_umma_z<64>(x, ldx, packed, scales, zeros, p, pl, st);
+        case 128: return launch_umma_z<128>(x, ldx, packed, scales, zeros, p, pl, st);
+        default: return launch_umma_z<256>(x, ldx, packed, scales, zeros, p, pl, st);
+    }
+}
+
+}  // namespace lq2

@@ -6,6 +6,10 @@
 // (qslab/kernels/gemlite/triton_kernels/gemm_splitK_A16fWnO16f_int32packing.py:199-412,
 //  gemm_A16fWnO16f_int32packing.py:174-373) behind the same buffers.
 //
+// Shared memory carries only what TMA delivered (about 2 bytes per packed byte); writing
+// fp16 weights to it and reading them back for the MMA would need 8 more and make the
+// kernel shared-memory-bound well below the HBM rate.
+//
 // Orientation.  The product is computed transposed, Y^T[n, m] = W[n, :] . X[m, :],
 // so that the 128 rows of the MMA are output channels and its N dimension
 // (16..256) is the batch: a 32-row decode batch wastes nothing.  Per CTA: 128
@@ -18,12 +22,12 @@
 //   warps 2-9   dequantise: thread (n, half) turns 4 packed words of channel n into
 //               4 x 8 fp16 values, (u - z) * s rounded once exactly as the reference
 //               (triton_kernels/utils.py:66-71; integer-valued zero points), and
-//               stores them as 16-byte chunks of the K-major, 128-byte-swizzled A
-//               tile; the nibble masks yield k in the order 0,4,1,5,2,6,3,7 inside
-//               a chunk, so the same threads permute the activation tile's chunks
-//               in place to match
-//   warp 1      issues tcgen05.mma (M=128, N=MB, K=16, fp32 accumulate in TMEM) and
-//               commits each stage to the mbarrier that frees its buffers
+//               stores them with tcgen05.st into the A tile in tensor memory (lane =
+//               channel, 32-bit column = two consecutive k): the 4x expanded
+//               weights never pass through shared memory
+//   warp 1      issues tcgen05.mma (M=128, N=MB, K=16, A from TMEM, B from shared
+//               memory, fp32 accumulate in TMEM) and commits each stage to the
+//               mbarriers that free its buffers
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator, then the same cluster
 //               split-K reduction through distributed shared memory as the
 //               streaming kernel, fp16 store
@@ -97,16 +101,26 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n.reg .pred p;\n"
-        "setp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
-}
 // arrive on an mbarrier once all MMAs issued so far by this thread have completed
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
+}
+// D[tmem] (+)= A[tmem] . B[smem]: the A operand (M = 128 lanes x K/2 columns, two fp16 per 32-bit
+// column, lower k in the lower half) is read from tensor memory
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// store 16 consecutive 32-bit columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]) : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
 // 16 consecutive accumulator columns of this thread's TMEM lane
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -135,27 +149,30 @@ __host__ __device__ constexpr uint32_t umma_idesc(int mma_m, int mma_n) {
     return (1u << 4) | (uint32_t(mma_n >> 3) << 17) | (uint32_t(mma_m >> 4) << 24);
 }
 
-// Two rings: a deep one for what TMA delivers (packed words, activations, scales: ~9 KB per
-// stage at MB = 32), which sets the bytes in flight, and a shallow one for the 16 KB
-// dequantised A tiles.
+// Two rings: one in shared memory for what TMA delivers (packed words, activations, scales:
+// ~9 KB per stage at MB = 32), which sets the bytes in flight, and one in tensor memory for
+// the dequantised A tiles (32 columns each), so the 4x expanded weights never touch shared
+// memory.
 template <int MB, int GPSU>
 struct ULayout {
-    static constexpr int A_BYTES = kUM * 128;                       // [128 n][64 k] fp16, swizzled
-    static constexpr int A_STAGES = 2;
+    static constexpr int A_STAGES = 3;
+    static constexpr int A_COLS = kUK / 2;                          // 32-bit TMEM columns per A tile (two fp16 each)
     static constexpr int X_BYTES = (MB * 128 + 1023) / 1024 * 1024; // [MB m][64 k] fp16, swizzled
     static constexpr int RAW_BYTES = 8 * kUM * 4;                   // [8 k8][128 n] int32
     static constexpr int S_BYTES = GPSU * kUM * 2;                  // [GPSU][128 n] fp16
     static constexpr int RAW_OFF = X_BYTES, S_OFF = RAW_OFF + RAW_BYTES, Z_OFF = S_OFF + S_BYTES;
     static constexpr int R_STAGE_BYTES = (Z_OFF + S_BYTES + 1023) / 1024 * 1024;   // x tile first: 1 KiB aligned
-    static constexpr int R_STAGES = MB <= 64 ? 4 : (MB <= 128 ? 4 : 3);
+    static constexpr int R_STAGES = MB <= 64 ? 6 : (MB <= 128 ? 4 : 3);
     static constexpr int TX_BYTES = MB * 128 + RAW_BYTES;           // + S_BYTES (x2 with zero points)
-    static constexpr int A_RING_OFF = 0, R_RING_OFF = A_STAGES * A_BYTES;
+    static constexpr int R_RING_OFF = 0;
     static constexpr int RING_BYTES = R_RING_OFF + R_STAGES * R_STAGE_BYTES;
     static constexpr int RED_BYTES = MB * kUM * 4;
     static constexpr int DATA_BYTES = RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES;
     static constexpr int NBARS = 2 * R_STAGES + 2 * A_STAGES + 1;
     static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + NBARS * 8 + 16;
-    static constexpr int TMEM_COLS = MB < 32 ? 32 : MB;
+    static constexpr int ACC_COLS = MB < 32 ? 32 : MB;
+    static constexpr int TMEM_NEED = ACC_COLS + A_STAGES * A_COLS;
+    static constexpr int TMEM_COLS = TMEM_NEED <= 64 ? 64 : (TMEM_NEED <= 128 ? 128 : (TMEM_NEED <= 256 ? 256 : 512));
 };
 
 template <int MB, bool ZTABLE, int GPSU>
@@ -205,7 +222,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    unsigned char* a_ring = smem + L::A_RING_OFF;
     unsigned char* r_ring = smem + L::R_RING_OFF;
 
     if (warp == 0) {
@@ -232,13 +248,13 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             mbar_wait_bounded(a_full(aslot), (it / AS) & 1);
             tc_fence_after();
             if (lane == 0) {
-                const uint32_t abase = smem_u32(a_ring + aslot * L::A_BYTES);
+                const uint32_t a_tmem = tmem_base + L::ACC_COLS + aslot * L::A_COLS;
                 const uint32_t xbase = smem_u32(r_ring + rslot * L::R_STAGE_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < kUK / 16; ++kk) {
-                    // a K step of 16 fp16 advances 32 bytes inside the 128-byte swizzled rows
-                    umma_f16(tmem_base, smem_desc_sw128(abase + kk * 32), smem_desc_sw128(xbase + kk * 32), idesc,
-                             (it > 0 || kk > 0) ? 1u : 0u);
+                    // a K step of 16 fp16: 8 TMEM columns of A, 32 bytes inside the swizzled rows of B
+                    umma_f16_ts(tmem_base, a_tmem + kk * 8, smem_desc_sw128(xbase + kk * 32), idesc,
+                                (it > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(a_free(aslot));                   // both buffers are reusable once these MMAs are done
                 umma_commit(raw_free(rslot));
@@ -248,55 +264,45 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
         }
     } else {
         // ------------------------------------------------------------ dequantise
-        const int d = tid - 64;
-        const int nl = d & (kUM - 1), half = d >> 7;          // channel within the tile, k8 rows 4*half..+3
+        // A warp reaches the 32 TMEM lanes of its quarter (warp % 4); lane = output channel.  Two
+        // warps share a quarter and take k8 rows 0-3 and 4-7 of the stage.
+        const int quarter = warp & 3, khalf = (warp - 2) >> 2;
+        const int nl = quarter * 32 + lane;
         const __half2 k16th = __floats2half2_rn(0.0625f, 0.0625f);
         const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
         const __half2 k64 = __floats2half2_rn(64.f, 64.f);
         for (int it = 0; it < my_stages; ++it) {
             const int rslot = it % RS, aslot = it % AS;
-            unsigned char* rbase = r_ring + rslot * L::R_STAGE_BYTES;
+            const unsigned char* rbase = r_ring + rslot * L::R_STAGE_BYTES;
             mbar_wait_bounded(raw_full(rslot), (it / RS) & 1);
-            if (it >= AS) mbar_wait_bounded(a_free(aslot), ((it / AS) - 1) & 1);
-            // ---- activation tile: k order inside every 16-byte chunk -> 0,4,1,5,2,6,3,7
-            for (int c = d; c < MB * 8; c += kDequantThreads) {
-                uint4* ptr = reinterpret_cast<uint4*>(rbase + c * 16);
-                const uint4 r = *ptr;
-                uint4 o;
-                o.x = __byte_perm(r.x, r.z, 0x5410);
-                o.y = __byte_perm(r.x, r.z, 0x7632);
-                o.z = __byte_perm(r.y, r.w, 0x5410);
-                o.w = __byte_perm(r.y, r.w, 0x7632);
-                *ptr = o;
+            if (it >= AS) {
+                mbar_wait_bounded(a_free(aslot), ((it / AS) - 1) & 1);
+                tc_fence_after();
             }
-            // ---- weights
             const uint32_t* raw = reinterpret_cast<const uint32_t*>(rbase + L::RAW_OFF);
             const __half* sc = reinterpret_cast<const __half*>(rbase + L::S_OFF);
             const __half* zc = reinterpret_cast<const __half*>(rbase + L::Z_OFF);
-            unsigned char* arow = a_ring + aslot * L::A_BYTES + (nl >> 3) * 1024 + (nl & 7) * 128;
-            __half2 s2, zlo, zhi;
-            auto load_meta = [&](int gq) {
-                s2 = __half2half2(sc[gq * kUM + nl]);
-                const __half2 z2 = ZTABLE ? __half2half2(zc[gq * kUM + nl]) : __floats2half2_rn(8.f, 8.f);
-                zlo = __hadd2(z2, k1024);
-                zhi = __hneg2(__hadd2(z2, k64));
-            };
-            if (GPSU == 1) load_meta(0);
+            const int gq = GPSU == 1 ? 0 : khalf;             // two groups of 32 per stage: rows 0-3, 4-7
+            const __half2 s2 = __half2half2(sc[gq * kUM + nl]);
+            const __half2 z2 = ZTABLE ? __half2half2(zc[gq * kUM + nl]) : __floats2half2_rn(8.f, 8.f);
+            const __half2 zlo = __hadd2(z2, k1024), zhi = __hneg2(__hadd2(z2, k64));
+            uint32_t cols[16];
 #pragma unroll
             for (int r4 = 0; r4 < 4; ++r4) {
-                const int r = 4 * half + r4;                  // k8 row inside the stage: k = 8r .. 8r+7
-                if (GPSU == 2 && r4 == 0) load_meta(half);    // two groups of 32 per stage: rows 0-3, 4-7
-                const uint32_t w = raw[r * kUM + nl];
+                const uint32_t w = raw[(4 * khalf + r4) * kUM + nl];     // k = 8r .. 8r+7 of channel nl
                 const uint32_t w8 = w >> 8;
-                uint4 o;
-                o.x = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w, 0x000f000fu, 0x64006400u)), zlo), s2));
-                o.y = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
-                o.z = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w8, 0x000f000fu, 0x64006400u)), zlo), s2));
-                o.w = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w8, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
-                *reinterpret_cast<uint4*>(arow + ((r ^ (nl & 7)) << 4)) = o;
+                // (u - z) * s rounded once; the masks give the pairs (0,4) (1,5) (2,6) (3,7)
+                const uint32_t v04 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w, 0x000f000fu, 0x64006400u)), zlo), s2));
+                const uint32_t v15 = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
+                const uint32_t v26 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w8, 0x000f000fu, 0x64006400u)), zlo), s2));
+                const uint32_t v37 = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w8, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
+                cols[4 * r4 + 0] = __byte_perm(v04, v15, 0x5410);        // k0 k1
+                cols[4 * r4 + 1] = __byte_perm(v26, v37, 0x5410);        // k2 k3
+                cols[4 * r4 + 2] = __byte_perm(v04, v15, 0x7632);        // k4 k5
+                cols[4 * r4 + 3] = __byte_perm(v26, v37, 0x7632);        // k6 k7
             }
-            // generic-proxy stores must be visible to the tensor core's (async proxy) reads
-            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            tmem_st16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + aslot * L::A_COLS + khalf * 16, cols);
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(a_full(aslot));
         }
@@ -389,7 +395,7 @@ struct UPlan {
 };
 
 // Batch tile and cluster size from shapes only: the largest power-of-two K split that
-// keeps the grid within one CTA per SM and leaves every rank at least four stages.
+// keeps the grid within one resident wave and leaves every rank at least four stages.
 UPlan make_uplan(int m, int n, int k) {
     UPlan p;
     p.mb = m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : (m <= 128 ? 128 : 256)));
@@ -398,7 +404,8 @@ UPlan make_uplan(int m, int n, int k) {
     const int stages = cdiv(k, kUK);
     const int base = p.n_tiles * p.m_tiles;
     int r = 1;
-    while (r < 8 && base * r * 2 <= kNumSMs * (p.mb <= 32 ? 3 : (p.mb <= 64 ? 2 : 1)) && stages / (r * 2) >= 4) r *= 2;
+    const int resident = kNumSMs * (p.mb <= 32 ? 3 : (p.mb <= 128 ? 2 : 1));
+    while (r < 8 && base * r * 2 <= resident && stages / (r * 2) >= 4) r *= 2;
     p.ranks = r;
     p.spr = cdiv(stages, r);
     return p;

@@ -373,6 +373,71 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def run_case(args):
+    """One small single-kernel case (inputs larger than L2, a few launches): the command that the
+    `ncu --set full` captures summarised under profiles/ run.  Prints one JSON line with the CUDA-event
+    time per launch (graph replay over distinct inputs, so nothing is served from L2)."""
+    import torch
+    from linkq2_b200.kernels.gemlite.ops import set_constant_weights
+    from linkq2_b200.kernels.kv4 import paged_attention_decode
+    from linkq2_b200.runtime.backends import make_quant_linear
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device; the operators have no CPU path")
+    torch.cuda.set_device(0)
+    g = torch.Generator().manual_seed(0)
+    peaks, which = measured_peaks()
+    if args.case in ("w4a16_gemv", "w4a16_m32"):
+        k, n, m, copies = 4096, 24576, (1 if args.case == "w4a16_gemv" else 32), 4
+        vals = (torch.randint(0, 16, (n, k), generator=g, dtype=torch.uint8).to(torch.int16) - 8).to(torch.int8)
+        scale = (torch.rand(n, k // 128, generator=g) * 0.01 + 0.001).half()
+        layers = [make_quant_linear("b200", vals, scale, group_size=128, symmetric=True, device="cuda",
+                                    dtype=torch.float16) for _ in range(copies)]
+        x = torch.randn(m, k, device="cuda", dtype=torch.float16)
+        torch.cuda.synchronize()
+        set_constant_weights(True)                     # as the runtime does once the checkpoint is loaded
+        calls = [lambda l=l: l(x) for l in layers]
+        nbytes = k * n // 2 + 2 * (k // 128) * n + 2 * m * (k + n)
+        what = f"gate_up geometry K={k} N={n} M={m}, {copies} distinct weight copies"
+    else:
+        hq, hkv, d, page, bs, ctx = 32, 8, 128, 256, 64, 4096
+        nb = bs * (ctx // page)
+        slots = nb * page
+        kq = torch.randint(-2**31, 2**31 - 1, (slots, hkv, d // 8), dtype=torch.int32, device="cuda")
+        vq = torch.randint(-2**31, 2**31 - 1, (slots, hkv, d // 8), dtype=torch.int32, device="cuda")
+        ks = (torch.rand(hkv, d, device="cuda") * 0.1 + 0.05).half()
+        vs = (torch.rand(slots, hkv, 2, device="cuda") * 0.1 + 0.05).half()
+        table = torch.randperm(nb, generator=g).int().view(bs, -1).cuda()
+        q = (torch.randn(bs, hq, d, device="cuda") * 0.5).half()
+        lens = torch.full((bs,), ctx, dtype=torch.int32, device="cuda")
+        calls = [lambda: paged_attention_decode(q, (kq, ks), (vq, vs), table, lens, block_n=page,
+                                                num_kv_heads=hkv)] * 3
+        nbytes = bs * ctx * hkv * (d + 2 * (d // 64)) + 4 * bs * hq * d
+        what = f"decode batch {bs}, context {ctx}, Qwen3-8B heads, page {page}, v_group 64 (277 MB of cache)"
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side), torch.inference_mode():
+        for c in calls:
+            c()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for c in calls:
+                c()
+        graph.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(side)
+        graph.replay()
+        b.record(side)
+        torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / len(calls)
+    gbs = nbytes / us / 1e3
+    print(json.dumps({"case": args.case, "workload": what, "launches_timed": len(calls),
+                      "us_per_launch": round(us, 2), "algorithmic_bytes_per_launch": nbytes,
+                      "achieved_gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 4), "of": which}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -382,8 +447,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the timed decode steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--case", default=None, choices=["w4a16_gemv", "w4a16_m32", "kv4_decode"],
+                    help="run one small single-kernel case instead of the workload (the profiled cases)")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

@@ -52,6 +52,24 @@ int lq2_abi_version(void);
 int lq2_w4_pack(const int8_t* values, int offset, int32_t* packed, int n, int k, void* stream);
 
 /*
+ * Declares the quantized weights constant (enabled != 0) or not (0, the
+ * default); returns the previous setting.  Process-wide.  No counterpart in
+ * the reference.
+ *
+ * Every kernel of this library is launched with programmatic stream
+ * serialization: it may be scheduled while the previous kernel of the stream is
+ * draining and waits for that kernel's completion before touching activations or
+ * outputs, so stream order is preserved for them.  With constant weights declared,
+ * lq2_w4a16_linear additionally starts fetching packed/scales/zeros BEFORE that
+ * wait.  The caller then guarantees that no kernel launched immediately before a
+ * lq2_w4a16_linear call on the same stream writes its packed, scales or zeros
+ * buffers - true for any inference loop once the checkpoint is loaded (the
+ * runtime enables it after loading; a memcpy, an event wait, a synchronize or
+ * any other kernel in between also restores the ordering).
+ */
+int lq2_w4a16_set_constant_weights(int enabled);
+
+/*
  * Bytes of scratch lq2_w4a16_linear needs for this problem size.  The current
  * kernels keep split-K partials on chip and need none (the answer is 0 and the
  * workspace argument may be NULL); the query stays in the ABI so that a caller

@@ -20,6 +20,7 @@ SIGNATURES = {
     "lq2_status_string": (c_char_p, [c_int]),
     "lq2_abi_version": (c_int, []),
     "lq2_w4_pack": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p]),
+    "lq2_w4a16_set_constant_weights": (c_int, [c_int]),
     "lq2_w4a16_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "lq2_w4a16_linear": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),

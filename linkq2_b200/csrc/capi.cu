@@ -25,6 +25,24 @@ size_t kv4_attention_counter_bytes(int, int);
 
 using namespace lq2;
 
+#include <atomic>
+#include <cstdlib>
+
+namespace {
+std::atomic<int> g_constant_weights{0};
+}  // namespace
+
+namespace lq2 {
+bool early_weight_fetch() { return g_constant_weights.load(std::memory_order_relaxed) != 0; }
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("LQ2_DISABLE_PDL");
+        return !(v && v[0] == '1');
+    }();
+    return on;
+}
+}  // namespace lq2
+
 namespace {
 inline bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 inline bool w4_shape_ok(int m, int n, int k, int group) {
@@ -58,6 +76,10 @@ int lq2_w4_pack(const int8_t* values, int offset, int32_t* packed, int n, int k,
     if (k % 8 || (offset != 0 && offset != 8)) return LQ2_ERR_SHAPE;
     if (!aligned(values, 8) || !aligned(packed, 4)) return LQ2_ERR_ALIGN;
     return w4_pack_launch(values, offset, packed, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int lq2_w4a16_set_constant_weights(int enabled) {
+    return g_constant_weights.exchange(enabled ? 1 : 0, std::memory_order_relaxed);
 }
 
 size_t lq2_w4a16_workspace_bytes(int m, int n, int k) {

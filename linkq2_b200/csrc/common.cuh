@@ -21,6 +21,56 @@ inline int check_launch() {
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// ---- Programmatic dependent launch.  Every kernel of this library is launched with the
+// "programmatic stream serialization" attribute and follows one protocol:
+//   * pdl_launch_dependents() as early as possible, but after any tensor-memory
+//     allocation (a dependent CTA that got the columns first would wait for this grid
+//     while this grid waits for the columns): once all CTAs of the grid have passed it,
+//     the next kernel of the stream may be scheduled onto free SM resources, so its
+//     launch latency and prologue overlap this grid's tail;
+//   * pdl_wait() before the first access to memory that an earlier kernel may have
+//     written, and before the first write to memory an earlier kernel may still read.
+//     It returns when all earlier grids have completed and their writes are visible.
+// Since every kernel waits before it completes, completion stays transitive along the
+// stream.  Kernels that are not launched with the attribute see both as no-ops.
+// The only accesses ever issued before pdl_wait() are loads of quantized weights and
+// their scales/zero points, and only after the caller has declared them constant
+// (lq2_w4a16_set_constant_weights; early_weight_fetch() below reads that switch).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+bool early_weight_fetch();   // defined next to the extern "C" switch
+bool pdl_enabled();          // false when the environment has LQ2_DISABLE_PDL=1 (diagnostic: plain stream order)
+
+// Launch `kernel` with the programmatic-serialization attribute (and, when cluster_y > 1,
+// as thread-block clusters of (1, cluster_y, 1)).
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      int cluster_y, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (cluster_y > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = cluster_y;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, kernel, KArgs(args)...) == cudaSuccess ? LQ2_OK : LQ2_ERR_CUDA;
+}
+
 // ---- warp-level tensor core op used as a dot-product engine by the
 // ---- bandwidth-bound kernels: D(16x8,f32) += A(16x16,f16) * B(16x8,f16)
 __device__ __forceinline__ void mma_m16n8k16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,

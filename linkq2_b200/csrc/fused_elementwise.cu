@@ -32,6 +32,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
     const __half* __restrict__ x, int64_t x_stride, const __half* __restrict__ residual,
     const __half* __restrict__ weight, __half* __restrict__ out, __half* __restrict__ residual_out,
     int hidden, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float partial[kNormThreads / 32];
     const int row = blockIdx.x, tid = threadIdx.x;
     const int chunks = hidden / 8;
@@ -92,6 +94,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __half* __restrict__ gate, int64_t g_stride,
                                                        const __half* __restrict__ up, int64_t u_stride,
                                                        __half* __restrict__ out, int rows, int width) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int chunks = width / 8;
     const int64_t id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (id >= int64_t(rows) * chunks) return;
@@ -137,6 +141,8 @@ __device__ __forceinline__ uint32_t kv_code(float x, float s) {
 
 template <int D>
 __global__ void __launch_bounds__(128) pre_attention_kernel(const PreAttnParams p) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int EPL = D / 64;              // elements per lane per half
     constexpr int HALF = D / 2;
     constexpr int LPW = 8 / EPL;             // lanes per packed word
@@ -275,10 +281,10 @@ int lq2_rmsnorm(const void* x, int64_t x_row_stride, const void* residual, const
     if (!aligned(x, 16) || x_row_stride % 8 || !aligned(weight, 16) || !aligned(out, 16) ||
         (residual && !aligned(residual, 16)) || (residual_out && !aligned(residual_out, 16)))
         return LQ2_ERR_ALIGN;
-    rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __half*>(x), x_row_stride, static_cast<const __half*>(residual),
-        static_cast<const __half*>(weight), static_cast<__half*>(out), static_cast<__half*>(residual_out), hidden, eps);
-    return check_launch();
+    return launch_pdl(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, static_cast<cudaStream_t>(stream), 1,
+                      static_cast<const __half*>(x), x_row_stride, static_cast<const __half*>(residual),
+                      static_cast<const __half*>(weight), static_cast<__half*>(out),
+                      static_cast<__half*>(residual_out), hidden, eps);
 }
 
 int lq2_silu_mul(const void* gate, int64_t gate_row_stride, const void* up, int64_t up_row_stride, void* out,
@@ -289,10 +295,9 @@ int lq2_silu_mul(const void* gate, int64_t gate_row_stride, const void* up, int6
     if (!aligned(gate, 16) || !aligned(up, 16) || !aligned(out, 16) || gate_row_stride % 8 || up_row_stride % 8)
         return LQ2_ERR_ALIGN;
     const int64_t total = int64_t(rows) * (width / 8);
-    silu_mul_kernel<<<int(cdiv64(total, 256)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __half*>(gate), gate_row_stride, static_cast<const __half*>(up), up_row_stride,
-        static_cast<__half*>(out), rows, width);
-    return check_launch();
+    return launch_pdl(silu_mul_kernel, dim3(unsigned(cdiv64(total, 256))), dim3(256), 0,
+                      static_cast<cudaStream_t>(stream), 1, static_cast<const __half*>(gate), gate_row_stride,
+                      static_cast<const __half*>(up), up_row_stride, static_cast<__half*>(out), rows, width);
 }
 
 int lq2_pre_attention(const void* q, const void* k, const void* v, int64_t q_stride, int64_t k_stride,
@@ -322,9 +327,8 @@ int lq2_pre_attention(const void* q, const void* k, const void* v, int64_t q_str
     const int64_t warps = int64_t(tokens) * (hq + hkv);
     const int blocks = int(cdiv64(warps, 4));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (d == 128) pre_attention_kernel<128><<<blocks, 128, 0, st>>>(p);
-    else pre_attention_kernel<64><<<blocks, 128, 0, st>>>(p);
-    return check_launch();
+    if (d == 128) return launch_pdl(pre_attention_kernel<128>, dim3(blocks), dim3(128), 0, st, 1, p);
+    return launch_pdl(pre_attention_kernel<64>, dim3(blocks), dim3(128), 0, st, 1, p);
 }
 
 }  // extern "C"

@@ -91,6 +91,8 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) { return h2_as_u32
 // RT: 16-row query tiles per (sequence, KV head): ceil(M * rep / 16), 3 rounded up to 4.
 template <int D, int RT>
 __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParams p) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int NW = D / 8;          // words per (token, head)
     constexpr int KWT = NW / 4;        // K words per lane per token (lanes t = 0..3 split the row)
     constexpr int VWT = NW / 8;        // V words per lane per token (lanes g = 0..7 split the row)
@@ -416,6 +418,8 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
 
 template <int D, int NG>
 __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const AttnParams p, const int hpc) {
+    pdl_launch_dependents();
+    pdl_wait();
     using L = FastLayout<D>;
     constexpr int NW = D / 8;             // words per (token, head)
     constexpr int KWT = NW / 4;           // K words per lane per token
@@ -883,21 +887,21 @@ int kv4_attention_launch(const __half* q, int64_t q_stride, const uint32_t* kq, 
             if (!ok) return LQ2_ERR_CUDA;
             configured[dev] = true;
         }
-        if (d == 128 && p.ng == 2) kv4_decode_fast_kernel<128, 2><<<fgrid, kFastThreads, FastLayout<128>::SMEM_BYTES, st>>>(p, hpc);
-        else if (d == 128) kv4_decode_fast_kernel<128, 1><<<fgrid, kFastThreads, FastLayout<128>::SMEM_BYTES, st>>>(p, hpc);
-        else kv4_decode_fast_kernel<64, 1><<<fgrid, kFastThreads, FastLayout<64>::SMEM_BYTES, st>>>(p, hpc);
-        return check_launch();
+        if (d == 128 && p.ng == 2)
+            return launch_pdl(kv4_decode_fast_kernel<128, 2>, fgrid, dim3(kFastThreads), FastLayout<128>::SMEM_BYTES, st, 1, p, hpc);
+        if (d == 128)
+            return launch_pdl(kv4_decode_fast_kernel<128, 1>, fgrid, dim3(kFastThreads), FastLayout<128>::SMEM_BYTES, st, 1, p, hpc);
+        return launch_pdl(kv4_decode_fast_kernel<64, 1>, fgrid, dim3(kFastThreads), FastLayout<64>::SMEM_BYTES, st, 1, p, hpc);
     }
     const int rt = row_tiles(m, hq, hkv);
     dim3 grid(p.splits, hkv, batch);
-#define LQ2_ATTN(DD, RR) kv4_attention_kernel<DD, RR><<<grid, kThreads, 0, st>>>(p)
+#define LQ2_ATTN(DD, RR) return launch_pdl(kv4_attention_kernel<DD, RR>, grid, dim3(kThreads), 0, st, 1, p)
     if (d == 128) {
         if (rt == 1) LQ2_ATTN(128, 1); else if (rt == 2) LQ2_ATTN(128, 2); else LQ2_ATTN(128, 4);
     } else {
         if (rt == 1) LQ2_ATTN(64, 1); else if (rt == 2) LQ2_ATTN(64, 2); else LQ2_ATTN(64, 4);
     }
 #undef LQ2_ATTN
-    return check_launch();
 }
 
 }  // namespace lq2

@@ -48,6 +48,8 @@ __global__ void __launch_bounds__(256) kv4_store_kernel(
     uint32_t* __restrict__ kq, const __half* __restrict__ ks, uint32_t* __restrict__ vq,
     __half* __restrict__ vs, const int32_t* __restrict__ slots, int tokens, int hkv, int nw,
     int words_per_group, int64_t num_slots) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const int per_token = hkv * nw;
     const bool active = id < int64_t(tokens) * per_token;
@@ -98,6 +100,8 @@ __global__ void __launch_bounds__(256) kv4_materialize_kernel(
     const uint32_t* __restrict__ kq, const __half* __restrict__ ks, const uint32_t* __restrict__ vq,
     const __half* __restrict__ vs, const int64_t* __restrict__ slots, __half* __restrict__ k_out,
     __half* __restrict__ v_out, int tokens, int hkv, int nw, int words_per_group, int64_t num_slots) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const int per_token = hkv * nw;
     if (id >= int64_t(tokens) * per_token) return;
@@ -137,12 +141,10 @@ int kv4_store_launch(const __half* k, const __half* v, int64_t k_stride, int64_t
     const int blocks = int(cdiv64(total, 256));
     const bool vec = aligned(k, 16) && aligned(v, 16) && k_stride % 8 == 0 && v_stride % 8 == 0;
     if (vec)
-        kv4_store_kernel<true><<<blocks, 256, 0, st>>>(k, v, k_stride, v_stride, kq, ks, vq, vs, slots,
-                                                       tokens, hkv, nw, wpg, num_slots);
-    else
-        kv4_store_kernel<false><<<blocks, 256, 0, st>>>(k, v, k_stride, v_stride, kq, ks, vq, vs, slots,
-                                                        tokens, hkv, nw, wpg, num_slots);
-    return check_launch();
+        return launch_pdl(kv4_store_kernel<true>, dim3(blocks), dim3(256), 0, st, 1, k, v, k_stride, v_stride, kq, ks,
+                          vq, vs, slots, tokens, hkv, nw, wpg, num_slots);
+    return launch_pdl(kv4_store_kernel<false>, dim3(blocks), dim3(256), 0, st, 1, k, v, k_stride, v_stride, kq, ks,
+                      vq, vs, slots, tokens, hkv, nw, wpg, num_slots);
 }
 
 int kv4_materialize_launch(const uint32_t* kq, const __half* ks, const uint32_t* vq, const __half* vs,
@@ -151,9 +153,8 @@ int kv4_materialize_launch(const uint32_t* kq, const __half* ks, const uint32_t*
     const int nw = d / 8, wpg = v_group / 8;
     const int64_t total = int64_t(tokens) * hkv * nw;
     const int blocks = int(cdiv64(total, 256));
-    kv4_materialize_kernel<<<blocks, 256, 0, st>>>(kq, ks, vq, vs, slots, k_out, v_out, tokens, hkv, nw,
-                                                   wpg, num_slots);
-    return check_launch();
+    return launch_pdl(kv4_materialize_kernel, dim3(blocks), dim3(256), 0, st, 1, kq, ks, vq, vs, slots, k_out, v_out,
+                      tokens, hkv, nw, wpg, num_slots);
 }
 
 }  // namespace lq2

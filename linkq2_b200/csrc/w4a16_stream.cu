@@ -65,6 +65,7 @@ struct W4Params {
     __half* y;
     int m, n, k, group;
     int stages_per_rank;
+    int early_weights;    // request weight bytes before the previous kernel of the stream has finished
 };
 
 // ---- mbarrier / bulk-copy primitives (shared::cta addresses as 32-bit values)
@@ -155,6 +156,7 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
     // stage a step must stay inside 4 consecutive rows instead.
     constexpr bool INTERLEAVE = GPS <= 2;
 
+    pdl_launch_dependents();
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // swizzle atoms are 1 KiB
     const uint32_t bars = smem_u32(smem + L::DATA_BYTES);    // full[STAGES], empty[STAGES]
@@ -192,28 +194,49 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
     constexpr int kpart = 0;
     if (warp == CONSUMERS) {
         // ------------------------------------------------------------ producer
-        for (int it = 0; it < my_stages; ++it) {
+        // Out-of-range rows and columns are zero-filled by the TMA unit and still count
+        // their full box size, so the expected byte count of a stage is a constant.
+        auto load_weights = [&](int it) {
             const int slot = it % STAGES, s = s0 + it;
-            if (it >= STAGES) mbar_wait(bars + 8 * (STAGES + slot), ((it / STAGES) - 1) & 1);
             const uint32_t full = bars + 8 * slot;
             const uint32_t base = smem_u32(smem + slot * L::STAGE_BYTES);
-            if (lane == 0) {
-                // Out-of-range rows and columns are zero-filled by the TMA unit and still
-                // count their full box size, so the expected byte count is a constant.
-                mbar_arrive_expect_tx(full, L::TX_BYTES + L::S_BYTES * (ZTABLE ? 2 : 1));
+            mbar_arrive_expect_tx(full, L::TX_BYTES + L::S_BYTES * (ZTABLE ? 2 : 1));
 #pragma unroll
-                for (int w = 0; w < WN; ++w)
-                    tma_load_2d(base + w * L::SLAB_BYTES, &map_w, tile_n0 + 32 * w, s * 16, full);
-                tma_load_2d(base + L::W_BYTES, &map_x, s * kStageK, m0, full);
-                tma_load_2d(base + L::W_BYTES + L::XBOX_BYTES, &map_x, s * kStageK + 64, m0, full);
-                const int gi = (GPS == 1) ? (s * kStageK) / p.group : s * GPS;
-                tma_load_2d(base + L::W_BYTES + L::X_BYTES, &map_s, tile_n0, gi, full);
-                if (ZTABLE) tma_load_2d(base + L::W_BYTES + L::X_BYTES + L::S_BYTES, &map_z, tile_n0, gi, full);
+            for (int w = 0; w < WN; ++w)
+                tma_load_2d(base + w * L::SLAB_BYTES, &map_w, tile_n0 + 32 * w, s * 16, full);
+            const int gi = (GPS == 1) ? (s * kStageK) / p.group : s * GPS;
+            tma_load_2d(base + L::W_BYTES + L::X_BYTES, &map_s, tile_n0, gi, full);
+            if (ZTABLE) tma_load_2d(base + L::W_BYTES + L::X_BYTES + L::S_BYTES, &map_z, tile_n0, gi, full);
+        };
+        auto load_activations = [&](int it) {
+            const int slot = it % STAGES, s = s0 + it;
+            const uint32_t full = bars + 8 * slot;
+            const uint32_t base = smem_u32(smem + slot * L::STAGE_BYTES);
+            tma_load_2d(base + L::W_BYTES, &map_x, s * kStageK, m0, full);
+            tma_load_2d(base + L::W_BYTES + L::XBOX_BYTES, &map_x, s * kStageK + 64, m0, full);
+        };
+        // When the caller has declared the weights constant, the first ring of weight bytes
+        // is requested before the previous kernel of the stream has finished; the
+        // activations, which that kernel may still be writing, only after pdl_wait().
+        const int ahead = min(my_stages, STAGES);
+        if (!p.early_weights) pdl_wait();
+        if (lane == 0)
+            for (int it = 0; it < ahead; ++it) load_weights(it);
+        if (p.early_weights) pdl_wait();
+        if (lane == 0)
+            for (int it = 0; it < ahead; ++it) load_activations(it);
+        __syncwarp();
+        for (int it = ahead; it < my_stages; ++it) {
+            mbar_wait(bars + 8 * (STAGES + it % STAGES), ((it / STAGES) - 1) & 1);
+            if (lane == 0) {
+                load_weights(it);
+                load_activations(it);
             }
             __syncwarp();
         }
     } else {
         // ------------------------------------------------------------ consumers
+        pdl_wait();
         float gacc[2][NJW][4];
         float xsum[NJW][4];
 #pragma unroll
@@ -462,19 +485,8 @@ int launch_one(const W4Params& p, const Plan& pl, cudaStream_t st) {
     ok = ok && make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ZTABLE ? p.zeros : p.scales, n, groups, n * 2,
                         L::TN, GPS, false);
     if (!ok) return LQ2_ERR_CUDA;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(pl.n_tiles, pl.ranks, pl.m_tiles);
-    cfg.blockDim = dim3(L::THREADS);
-    cfg.dynamicSmemBytes = L::SMEM_BYTES;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = pl.ranks;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, map_w, map_x, map_s, map_z, p) == cudaSuccess ? LQ2_OK : LQ2_ERR_CUDA;
+    return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(L::THREADS), L::SMEM_BYTES, st, pl.ranks,
+                      map_w, map_x, map_s, map_z, p);
 }
 
 template <int NJ, bool ZTABLE, int GPS>
@@ -509,6 +521,7 @@ int w4a16_stream_launch(const __half* x, int64_t ldx, const int32_t* packed, con
     p.x = x; p.ldx = ldx; p.packed = packed; p.scales = scales; p.zeros = zeros; p.y = y;
     p.m = m; p.n = n; p.k = k; p.group = group;
     p.stages_per_rank = pl.spr;
+    p.early_weights = early_weight_fetch() ? 1 : 0;
     switch (pl.nj) {
         case 1: return launch_z<1>(p, pl, st);
         case 2: return launch_z<2>(p, pl, st);

@@ -1,6 +1,6 @@
 // W4A16 linear for M > 8 (batched decode, verify, prefill): int4 weights are
-// dequantised into shared memory and multiplied on the 5th-generation tensor
-// cores (tcgen05.mma) with the accumulator in tensor memory.
+// dequantised into tensor memory and multiplied on the 5th-generation tensor
+// cores (tcgen05.mma) with the accumulator in tensor memory as well.
 //
 // Replaces the split-K and large-M Triton routes of the reference
 // (qslab/kernels/gemlite/triton_kernels/gemm_splitK_A16fWnO16f_int32packing.py:199-412,
@@ -44,7 +44,11 @@ namespace lq2 {
 namespace {
 
 constexpr int kUM = 128;          // output channels per CTA (MMA M)
-constexpr int kUK = 64;           // k per stage
+// k per pipeline stage (64 or 128)
+#ifndef LQ2_UMMA_SMALL_STAGE_K
+#define LQ2_UMMA_SMALL_STAGE_K 64
+#endif
+__host__ __device__ constexpr int stage_k(int mb) { return mb <= 64 ? LQ2_UMMA_SMALL_STAGE_K : 64; }
 constexpr int kUThreads = 320;    // 10 warps
 constexpr int kDequantThreads = 256;
 
@@ -52,6 +56,7 @@ struct UParams {
     __half* y;
     int m, n, k, group;
     int stages_per_rank;
+    int early_weights;    // request weight bytes before the previous kernel of the stream has finished
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -114,13 +119,12 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
         ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
-// store 16 consecutive 32-bit columns of this thread's TMEM lane
+// store 16 consecutive 32-bit columns of this thread's TMEM lane (completion: tcgen05.wait::st)
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
         ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]) : "memory");
-    asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
 // 16 consecutive accumulator columns of this thread's TMEM lane
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -155,15 +159,17 @@ __host__ __device__ constexpr uint32_t umma_idesc(int mma_m, int mma_n) {
 // memory.
 template <int MB, int GPSU>
 struct ULayout {
+    static constexpr int UK = stage_k(MB);
     static constexpr int A_STAGES = 3;
-    static constexpr int A_COLS = kUK / 2;                          // 32-bit TMEM columns per A tile (two fp16 each)
-    static constexpr int X_BYTES = (MB * 128 + 1023) / 1024 * 1024; // [MB m][64 k] fp16, swizzled
-    static constexpr int RAW_BYTES = 8 * kUM * 4;                   // [8 k8][128 n] int32
+    static constexpr int A_COLS = UK / 2;                           // 32-bit TMEM columns per A tile (two fp16 each)
+    static constexpr int XBOX_BYTES = (MB * 128 + 1023) / 1024 * 1024;   // [MB m][64 k] fp16, swizzled
+    static constexpr int X_BYTES = (UK / 64) * XBOX_BYTES;
+    static constexpr int RAW_BYTES = (UK / 8) * kUM * 4;            // [UK/8 k8][128 n] int32
     static constexpr int S_BYTES = GPSU * kUM * 2;                  // [GPSU][128 n] fp16
     static constexpr int RAW_OFF = X_BYTES, S_OFF = RAW_OFF + RAW_BYTES, Z_OFF = S_OFF + S_BYTES;
     static constexpr int R_STAGE_BYTES = (Z_OFF + S_BYTES + 1023) / 1024 * 1024;   // x tile first: 1 KiB aligned
-    static constexpr int R_STAGES = MB <= 64 ? 6 : (MB <= 128 ? 4 : 3);
-    static constexpr int TX_BYTES = MB * 128 + RAW_BYTES;           // + S_BYTES (x2 with zero points)
+    static constexpr int R_STAGES = UK == 128 ? (MB <= 16 ? 4 : 3) : (MB <= 64 ? 6 : (MB <= 128 ? 4 : 3));
+    static constexpr int TX_BYTES = (UK / 64) * MB * 128 + RAW_BYTES;   // + S_BYTES (x2 with zero points)
     static constexpr int R_RING_OFF = 0;
     static constexpr int RING_BYTES = R_RING_OFF + R_STAGES * R_STAGE_BYTES;
     static constexpr int RED_BYTES = MB * kUM * 4;
@@ -173,6 +179,8 @@ struct ULayout {
     static constexpr int ACC_COLS = MB < 32 ? 32 : MB;
     static constexpr int TMEM_NEED = ACC_COLS + A_STAGES * A_COLS;
     static constexpr int TMEM_COLS = TMEM_NEED <= 64 ? 64 : (TMEM_NEED <= 128 ? 128 : (TMEM_NEED <= 256 ? 256 : 512));
+    static_assert(TMEM_NEED <= 512, "tensor memory has 512 columns");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
 template <int MB, bool ZTABLE, int GPSU>
@@ -183,7 +191,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     using L = ULayout<MB, GPSU>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    constexpr int RS = L::R_STAGES, AS = L::A_STAGES;
+    constexpr int RS = L::R_STAGES, AS = L::A_STAGES, UK = L::UK;
     const uint32_t bars = smem_u32(smem + L::DATA_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::DATA_BYTES + L::NBARS * 8);
     auto raw_full = [&](int s) { return bars + 8 * s; };               // TMA bytes of raw stage s landed
@@ -196,7 +204,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     const int tile_n0 = blockIdx.x * kUM;
     const int m0 = blockIdx.z * MB;
     const int rows = min(MB, p.m - m0);
-    const int total_stages = (p.k + kUK - 1) / kUK;
+    const int total_stages = (p.k + UK - 1) / UK;
     const int ranks = gridDim.y, rank = blockIdx.y;
     const int s0 = min(total_stages, rank * p.stages_per_rank);
     const int s1 = min(total_stages, s0 + p.stages_per_rank);
@@ -221,27 +229,53 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Only now may the next kernel of the stream be scheduled next to this CTA: had it been let in
+    // before the allocation above, its CTAs could take the tensor memory this one still needs and then
+    // wait for this grid to finish.
+    pdl_launch_dependents();
     const uint32_t tmem_base = *tmem_slot;
     unsigned char* r_ring = smem + L::R_RING_OFF;
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
-        for (int it = 0; it < my_stages; ++it) {
+        auto load_weights = [&](int it) {
             const int slot = it % RS, s = s0 + it;
-            if (it >= RS) mbar_wait_bounded(raw_free(slot), ((it / RS) - 1) & 1);
+            const uint32_t base = smem_u32(r_ring + slot * L::R_STAGE_BYTES);
+            mbar_arrive_expect_tx(raw_full(slot), L::TX_BYTES + L::S_BYTES * (ZTABLE ? 2 : 1));
+            tma_load_2d(base + L::RAW_OFF, &map_w, tile_n0, s * (UK / 8), raw_full(slot));
+            const int gi = (GPSU == 1) ? (s * UK) / p.group : s * GPSU;
+            tma_load_2d(base + L::S_OFF, &map_s, tile_n0, gi, raw_full(slot));
+            if (ZTABLE) tma_load_2d(base + L::Z_OFF, &map_z, tile_n0, gi, raw_full(slot));
+        };
+        auto load_activations = [&](int it) {
+            const int slot = it % RS, s = s0 + it;
+            const uint32_t base = smem_u32(r_ring + slot * L::R_STAGE_BYTES);
+#pragma unroll
+            for (int b = 0; b < UK / 64; ++b)
+                tma_load_2d(base + b * L::XBOX_BYTES, &map_x, s * UK + 64 * b, m0, raw_full(slot));
+        };
+        // When the caller has declared the weights constant, the first ring of weight bytes
+        // is requested before the previous kernel of the stream has finished; the
+        // activations, which that kernel may still be writing, only after pdl_wait().
+        const int ahead = min(my_stages, RS);
+        if (!p.early_weights) pdl_wait();
+        if (lane == 0)
+            for (int it = 0; it < ahead; ++it) load_weights(it);
+        if (p.early_weights) pdl_wait();
+        if (lane == 0)
+            for (int it = 0; it < ahead; ++it) load_activations(it);
+        __syncwarp();
+        for (int it = ahead; it < my_stages; ++it) {
+            mbar_wait_bounded(raw_free(it % RS), ((it / RS) - 1) & 1);
             if (lane == 0) {
-                const uint32_t base = smem_u32(r_ring + slot * L::R_STAGE_BYTES);
-                mbar_arrive_expect_tx(raw_full(slot), L::TX_BYTES + L::S_BYTES * (ZTABLE ? 2 : 1));
-                tma_load_2d(base + L::RAW_OFF, &map_w, tile_n0, s * 8, raw_full(slot));
-                tma_load_2d(base, &map_x, s * kUK, m0, raw_full(slot));
-                const int gi = (GPSU == 1) ? (s * kUK) / p.group : s * GPSU;
-                tma_load_2d(base + L::S_OFF, &map_s, tile_n0, gi, raw_full(slot));
-                if (ZTABLE) tma_load_2d(base + L::Z_OFF, &map_z, tile_n0, gi, raw_full(slot));
+                load_weights(it);
+                load_activations(it);
             }
             __syncwarp();
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        pdl_wait();
         constexpr uint32_t idesc = umma_idesc(kUM, MB);
         for (int it = 0; it < my_stages; ++it) {
             const int rslot = it % RS, aslot = it % AS;
@@ -251,9 +285,11 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                 const uint32_t a_tmem = tmem_base + L::ACC_COLS + aslot * L::A_COLS;
                 const uint32_t xbase = smem_u32(r_ring + rslot * L::R_STAGE_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < kUK / 16; ++kk) {
+                for (int kk = 0; kk < UK / 16; ++kk) {
                     // a K step of 16 fp16: 8 TMEM columns of A, 32 bytes inside the swizzled rows of B
-                    umma_f16_ts(tmem_base, a_tmem + kk * 8, smem_desc_sw128(xbase + kk * 32), idesc,
+                    // (a 64-k box holds four such steps)
+                    umma_f16_ts(tmem_base, a_tmem + kk * 8,
+                                smem_desc_sw128(xbase + (kk >> 2) * L::XBOX_BYTES + (kk & 3) * 32), idesc,
                                 (it > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(a_free(aslot));                   // both buffers are reusable once these MMAs are done
@@ -264,6 +300,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
         }
     } else {
         // ------------------------------------------------------------ dequantise
+        pdl_wait();
         // A warp reaches the 32 TMEM lanes of its quarter (warp % 4); lane = output channel.  Two
         // warps share a quarter and take k8 rows 0-3 and 4-7 of the stage.
         const int quarter = warp & 3, khalf = (warp - 2) >> 2;
@@ -271,41 +308,63 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
         const __half2 k16th = __floats2half2_rn(0.0625f, 0.0625f);
         const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
         const __half2 k64 = __floats2half2_rn(64.f, 64.f);
+        constexpr int W = UK / 16;                            // packed words per thread per stage
+        // The stores of a stage are left in flight while the next stage's words are fetched
+        // from shared memory; only then are they waited for and the tile handed to the MMA warp.
+        auto publish = [&](int it_done) {
+            asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(a_full(it_done % AS));
+        };
         for (int it = 0; it < my_stages; ++it) {
             const int rslot = it % RS, aslot = it % AS;
             const unsigned char* rbase = r_ring + rslot * L::R_STAGE_BYTES;
             mbar_wait_bounded(raw_full(rslot), (it / RS) & 1);
+            const uint32_t* raw = reinterpret_cast<const uint32_t*>(rbase + L::RAW_OFF);
+            const __half* sc = reinterpret_cast<const __half*>(rbase + L::S_OFF);
+            const __half* zc = reinterpret_cast<const __half*>(rbase + L::Z_OFF);
+            uint32_t wv[W];
+#pragma unroll
+            for (int r = 0; r < W; ++r) wv[r] = raw[(W * khalf + r) * kUM + nl];   // k = 8 * row .. + 7 of channel nl
+            // quantization group of each block of four words (32 k); a thread covers UK/2 consecutive k
+            __half sraw[W / 4], zraw[W / 4];
+#pragma unroll
+            for (int b = 0; b < W / 4; ++b) {
+                const int gq = ((W * khalf + 4 * b) * 8 * GPSU) / UK;
+                sraw[b] = sc[gq * kUM + nl];
+                zraw[b] = ZTABLE ? zc[gq * kUM + nl] : __float2half_rn(8.f);
+            }
+            if (it > 0) publish(it - 1);
             if (it >= AS) {
                 mbar_wait_bounded(a_free(aslot), ((it / AS) - 1) & 1);
                 tc_fence_after();
             }
-            const uint32_t* raw = reinterpret_cast<const uint32_t*>(rbase + L::RAW_OFF);
-            const __half* sc = reinterpret_cast<const __half*>(rbase + L::S_OFF);
-            const __half* zc = reinterpret_cast<const __half*>(rbase + L::Z_OFF);
-            const int gq = GPSU == 1 ? 0 : khalf;             // two groups of 32 per stage: rows 0-3, 4-7
-            const __half2 s2 = __half2half2(sc[gq * kUM + nl]);
-            const __half2 z2 = ZTABLE ? __half2half2(zc[gq * kUM + nl]) : __floats2half2_rn(8.f, 8.f);
-            const __half2 zlo = __hadd2(z2, k1024), zhi = __hneg2(__hadd2(z2, k64));
-            uint32_t cols[16];
 #pragma unroll
-            for (int r4 = 0; r4 < 4; ++r4) {
-                const uint32_t w = raw[(4 * khalf + r4) * kUM + nl];     // k = 8r .. 8r+7 of channel nl
-                const uint32_t w8 = w >> 8;
-                // (u - z) * s rounded once; the masks give the pairs (0,4) (1,5) (2,6) (3,7)
-                const uint32_t v04 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w, 0x000f000fu, 0x64006400u)), zlo), s2));
-                const uint32_t v15 = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
-                const uint32_t v26 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w8, 0x000f000fu, 0x64006400u)), zlo), s2));
-                const uint32_t v37 = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w8, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
-                cols[4 * r4 + 0] = __byte_perm(v04, v15, 0x5410);        // k0 k1
-                cols[4 * r4 + 1] = __byte_perm(v26, v37, 0x5410);        // k2 k3
-                cols[4 * r4 + 2] = __byte_perm(v04, v15, 0x7632);        // k4 k5
-                cols[4 * r4 + 3] = __byte_perm(v26, v37, 0x7632);        // k6 k7
+            for (int b = 0; b < W / 4; ++b) {
+                const __half2 s2 = __half2half2(sraw[b]);
+                const __half2 z2 = __half2half2(zraw[b]);
+                const __half2 zlo = __hadd2(z2, k1024), zhi = __hneg2(__hadd2(z2, k64));
+                uint32_t cols[16];
+#pragma unroll
+                for (int r4 = 0; r4 < 4; ++r4) {
+                    const uint32_t w = wv[4 * b + r4];
+                    const uint32_t w8 = w >> 8;
+                    // (u - z) * s rounded once; the masks give the pairs (0,4) (1,5) (2,6) (3,7)
+                    const uint32_t v04 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w, 0x000f000fu, 0x64006400u)), zlo), s2));
+                    const uint32_t v15 = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
+                    const uint32_t v26 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(w8, 0x000f000fu, 0x64006400u)), zlo), s2));
+                    const uint32_t v37 = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(w8, 0x00f000f0u, 0x64006400u)), k16th, zhi), s2));
+                    cols[4 * r4 + 0] = __byte_perm(v04, v15, 0x5410);        // k0 k1
+                    cols[4 * r4 + 1] = __byte_perm(v26, v37, 0x5410);        // k2 k3
+                    cols[4 * r4 + 2] = __byte_perm(v04, v15, 0x7632);        // k4 k5
+                    cols[4 * r4 + 3] = __byte_perm(v26, v37, 0x7632);        // k6 k7
+                }
+                tmem_st16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + aslot * L::A_COLS +
+                              khalf * (UK / 4) + 16 * b, cols);
             }
-            tmem_st16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + aslot * L::A_COLS + khalf * 16, cols);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(a_full(aslot));
         }
+        if (my_stages > 0) publish(my_stages - 1);
     }
 
     // ---- epilogue: warps 2-5 read the accumulator (TMEM lane = output channel)
@@ -401,7 +460,7 @@ UPlan make_uplan(int m, int n, int k) {
     p.mb = m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : (m <= 128 ? 128 : 256)));
     p.m_tiles = cdiv(m, p.mb);
     p.n_tiles = cdiv(n, kUM);
-    const int stages = cdiv(k, kUK);
+    const int stages = cdiv(k, stage_k(p.mb));
     const int base = p.n_tiles * p.m_tiles;
     int r = 1;
     const int resident = kNumSMs * (p.mb <= 32 ? 3 : (p.mb <= 128 ? 2 : 1));
@@ -426,31 +485,23 @@ int launch_umma(const __half* x, int64_t ldx, const int32_t* packed, const __hal
     }
     alignas(64) CUtensorMap map_w, map_x, map_s, map_z;
     const uint64_t n = uint64_t(p.n), k = uint64_t(p.k), groups = uint64_t(p.k / p.group);
-    bool ok = make_map(&map_w, CU_TENSOR_MAP_DATA_TYPE_INT32, packed, n, k / 8, n * 4, kUM, 8, false);
+    bool ok = make_map(&map_w, CU_TENSOR_MAP_DATA_TYPE_INT32, packed, n, k / 8, n * 4, kUM, L::UK / 8, false);
     ok = ok && make_map(&map_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, uint64_t(p.m), uint64_t(ldx) * 2, 64, MB, true);
     ok = ok && make_map(&map_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales, n, groups, n * 2, kUM, GPSU, false);
     ok = ok && make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ZTABLE ? zeros : scales, n, groups, n * 2, kUM, GPSU, false);
     if (!ok) return LQ2_ERR_CUDA;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(pl.n_tiles, pl.ranks, pl.m_tiles);
-    cfg.blockDim = dim3(kUThreads);
-    cfg.dynamicSmemBytes = L::SMEM_BYTES;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = pl.ranks;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, map_w, map_x, map_s, map_z, p) == cudaSuccess ? LQ2_OK : LQ2_ERR_CUDA;
+    return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(kUThreads), L::SMEM_BYTES, st, pl.ranks,
+                      map_w, map_x, map_s, map_z, p);
 }
 
 template <int MB, bool ZTABLE>
 int launch_umma_g(const __half* x, int64_t ldx, const int32_t* packed, const __half* scales, const __half* zeros,
                   const UParams& p, const UPlan& pl, cudaStream_t st) {
-    if (p.group >= 64) return launch_umma<MB, ZTABLE, 1>(x, ldx, packed, scales, zeros, p, pl, st);
-    return launch_umma<MB, ZTABLE, 2>(x, ldx, packed, scales, zeros, p, pl, st);
+    constexpr int UK = stage_k(MB);                    // groups per stage: 1, 2 or 4
+    if (p.group >= UK) return launch_umma<MB, ZTABLE, 1>(x, ldx, packed, scales, zeros, p, pl, st);
+    if (p.group * 2 == UK) return launch_umma<MB, ZTABLE, 2>(x, ldx, packed, scales, zeros, p, pl, st);
+    if constexpr (UK == 128) return launch_umma<MB, ZTABLE, 4>(x, ldx, packed, scales, zeros, p, pl, st);
+    return LQ2_ERR_SHAPE;
 }
 
 template <int MB>
@@ -468,6 +519,7 @@ int w4a16_umma_launch(const __half* x, int64_t ldx, const int32_t* packed, const
     if (pl.m_tiles > 65535) return LQ2_ERR_SHAPE;
     UParams p;
     p.y = y; p.m = m; p.n = n; p.k = k; p.group = group; p.stages_per_rank = pl.spr;
+    p.early_weights = early_weight_fetch() ? 1 : 0;
     switch (pl.mb) {
         case 16: return launch_umma_z<16>(x, ldx, packed, scales, zeros, p, pl, st);
         case 32: return launch_umma_z<32>(x, ldx, packed, scales, zeros, p, pl, st);

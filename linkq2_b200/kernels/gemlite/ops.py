@@ -8,6 +8,14 @@ import torch
 from linkq2_b200 import _lib, _workspace
 
 
+def set_constant_weights(enabled: bool) -> bool:
+    """Declare the quantized weights constant (``lq2_w4a16_set_constant_weights``): ``linear``
+    may then start fetching ``packed``/``scales``/``zeros`` before the previous kernel of the
+    stream has finished.  Returns the previous setting.  Launches recorded into a CUDA graph
+    keep the setting they were captured with."""
+    return bool(_lib.lib.lq2_w4a16_set_constant_weights(1 if enabled else 0))
+
+
 def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
            meta) -> torch.Tensor:
     """``x [..., K] fp16`` times the dequantised ``[K, N]`` weight -> ``[..., N] fp16``.

@@ -17,6 +17,14 @@ from linkq2_b200.runtime.backends.base import QuantLinear
 _FP32, _FP16 = 0, 1
 
 
+def _weights_complete(device):
+    """Load-time barrier: the kernels that built the buffers have finished before the
+    layer can be called.  With constant weights declared (``set_constant_weights``) the
+    linear kernels fetch weight bytes ahead of stream order, so a layer must never be
+    called while the kernels that wrote its buffers may still be running."""
+    torch.cuda.current_stream(device).synchronize()
+
+
 class B200Linear(QuantLinear):
     @classmethod
     @torch.no_grad()
@@ -44,6 +52,7 @@ class B200Linear(QuantLinear):
         layer.register_buffer("input_scale", None if input_scale is None
                               else input_scale.to(device=device, dtype=dtype))
         layer._meta = (4, group_size, 15, 8, _FP16, _FP16, _FP32, _FP16, 0, 3, True, 104)
+        _weights_complete(layer.packed.device)
         return layer
 
     @classmethod
@@ -72,6 +81,7 @@ class B200Linear(QuantLinear):
                               else torch.cat([l.zeros for l in layers], dim=1).contiguous())
         fused.register_buffer("input_scale", None)
         fused._meta = first._meta
+        _weights_complete(fused.packed.device)
         return fused
 
     def forward(self, x):

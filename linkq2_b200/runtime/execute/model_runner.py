@@ -14,6 +14,7 @@ from dataclasses import dataclass
 
 import torch
 
+from linkq2_b200.kernels.gemlite.ops import set_constant_weights
 from linkq2_b200.runtime.execute.cuda_graph import CUDAGraphs
 from linkq2_b200.runtime.model.context import get_context, reset_context, set_context
 from linkq2_b200.runtime.parallel import get_tp
@@ -44,6 +45,11 @@ class ModelRunner:
         self.last_logits = None
         self.allocate_kv_cache()
         self.load_smoothing(smooth_kv)
+        # The checkpoint is loaded and nothing writes the quantized weights from here on:
+        # let the linear kernels fetch them ahead of stream order (before graph capture,
+        # which records the setting with each launch).
+        torch.cuda.synchronize(self.device)
+        set_constant_weights(True)
         self.cuda_graphs = None
         if not config.enforce_eager:
             self.cuda_graphs = CUDAGraphs(

@@ -10,7 +10,7 @@
 // Data movement.  A CTA owns 32*WN output columns and a contiguous range of K.
 // One producer warp keeps a ring of STAGES shared-memory buffers (128 k each)
 // full with tiled TMA loads (cp.async.bulk.tensor, 128-byte swizzle, no
-// multicast) of packed words, activations, scales and zero points, signalled
+// cluster-wide broadcast) of packed words, activations, scales and zero points, signalled
 // through mbarriers; WN consumer warps wait on a stage, use it and hand it back.
 // Rows or columns past the end of a tensor are zero-filled by the TMA unit.  The
 // bytes in flight per SM are set by the ring depth, and the main loop has no
@@ -100,7 +100,7 @@ __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity) {
         if (mbar_try_wait(bar, parity)) return;
     atomicAdd(&g_lq2_w4_wait_timeouts, 1u);
 }
-// 2-D tiled TMA load (no multicast): box at element coordinates (c0 = innermost, c1) -> shared memory
+// 2-D tiled TMA load (one CTA is the only receiver): box at element coordinates (c0 = innermost, c1) -> shared memory
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"

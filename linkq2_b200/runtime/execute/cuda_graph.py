@@ -83,6 +83,17 @@ class CUDAGraphs:
                 reset_context()
             self.families[rows] = GraphFamily(graphs, buffers)
 
+    def release(self):
+        """Destroy the captured graphs.  Under tensor parallelism they hold the NCCL
+        communicator's kernels, and the graphs must be gone before the process group
+        is destroyed (or the interpreter tears it down at exit), else that teardown
+        can block."""
+        torch.cuda.synchronize(self.device)
+        for family in self.families.values():
+            family.graphs.clear()
+        self.families.clear()
+        self.pool = None
+
     def stage(self, input_ids, positions, slot_mapping, context_lens, block_tables, rows=1):
         """Copy one step's metadata into the fixed buffers; returns the batch bucket."""
         b = self.families[rows].buffers

@@ -58,6 +58,13 @@ class ModelRunner:
                 verify_rows=config.spec_num_drafts + 1, device=self.device)
             self.cuda_graphs.capture(self._forward)
 
+    def shutdown(self):
+        """Release the CUDA graphs (call on every rank before the process group is
+        destroyed; harmless otherwise)."""
+        if self.cuda_graphs is not None:
+            self.cuda_graphs.release()
+            self.cuda_graphs = None
+
     # ---- pool ---------------------------------------------------------------
     def allocate_kv_cache(self):
         cfg, mc = self.config, self.model.config

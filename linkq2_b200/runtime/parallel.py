@@ -68,6 +68,18 @@ def init_from_env(backend: str | None = None) -> TensorParallel:
     return get_tp()
 
 
+def shutdown():
+    """Orderly end of a multi-rank run: every rank reaches this point, then the
+    process group is destroyed.  Captured CUDA graphs that contain collectives must
+    have been released before (``ModelRunner.shutdown``)."""
+    if dist.is_available() and dist.is_initialized():
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    set_tp(TensorParallel())
+
+
 # ---- sharding of logical quantized tensors ---------------------------------
 COLUMN, ROW = "column", "row"
 

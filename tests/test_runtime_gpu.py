@@ -18,12 +18,12 @@ PROJ = ["self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o
         "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"]
 
 
-def write_checkpoint(path, affine=False, seed=7):
+def write_checkpoint(path, affine=False, seed=7, hq=2, hkv=1):
     """A W4 checkpoint in the reference's layout (compression/checkpoint.py:33-63)
     plus the dense fp32 weights the CPU oracle runs on."""
     from safetensors.torch import save_file
     g = torch.Generator().manual_seed(seed)
-    hid, inter, hq, hkv, d = 128, 256, 2, 1, 64
+    hid, inter, d = 128, 256, 64
     shapes = {"self_attn.q_proj": (hq * d, hid), "self_attn.k_proj": (hkv * d, hid),
               "self_attn.v_proj": (hkv * d, hid), "self_attn.o_proj": (hid, hq * d),
               "mlp.gate_proj": (inter, hid), "mlp.up_proj": (inter, hid), "mlp.down_proj": (hid, inter)}
@@ -64,7 +64,7 @@ def write_checkpoint(path, affine=False, seed=7):
     path.mkdir()
     save_file(tensors, str(path / "model.safetensors"))
     method = "awq_affine_w4a16" if affine else "rtn_w4a16"
-    (path / "config.json").write_text(json.dumps(dict(CFG, quantization_config={
+    (path / "config.json").write_text(json.dumps(dict(CFG, num_attention_heads=hq, num_key_value_heads=hkv, quantization_config={
         "quant_method": method, "bits": 4, "group_size": 128, "symmetric": not affine})))
     (path / "quantized_layers.json").write_text(json.dumps(layers))
     weights = {k: v for k, v in tensors.items() if v.dtype == torch.float16 and k.count(".weight") == 1

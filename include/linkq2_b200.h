@@ -248,6 +248,64 @@ int lq2_pre_attention(const void* q, const void* k, const void* v, int64_t q_str
                       uint32_t* vq, void* vs, const int32_t* slots, int tokens, int hq, int hkv, int d,
                       int v_group, int64_t num_slots, float eps, void* stream);
 
+/* --------------------------------------------------------------------------
+ * Tensor-parallel exchange.  No counterpart in the reference, which is
+ * single-GPU (qslab/runtime/model/qwen3.py:1-5): the sum all-reduce of the
+ * [M, hidden] fp16 activations that the row-split o_proj and down_proj
+ * (qwen3.py:53,64) need when the layers are sharded over the GPUs of one
+ * NVSwitch domain, one process per GPU.  One kernel per rank over peer memory;
+ * a message is pushed into every peer's buffer and summed there in rank order
+ * (fp32), so all ranks obtain identical bits.
+ *
+ * Setup, once per process: every rank creates one exchange buffer, hands its
+ * 64-byte handle to the other ranks (any host channel), opens theirs, and
+ * passes the table of world pointers, its own at index rank, to every call.
+ * All ranks must issue the same sequence of lq2_allreduce_fp16 calls (same
+ * counts), each rank on one stream.  These setup calls are the only entry
+ * points of the library that allocate device memory or synchronise.
+ * -------------------------------------------------------------------------- */
+
+/* Size of the exchange buffer for `world` ranks (2..8) and messages of up to
+ * max_message_bytes (a multiple of 16); 0 for unsupported arguments. */
+size_t lq2_allreduce_buffer_bytes(int world, size_t max_message_bytes);
+
+/* Allocates (cudaMalloc) and zero-fills this rank's buffer on the current device
+ * and writes its CUDA IPC handle (64 bytes) to ipc_handle_64. */
+int lq2_allreduce_buffer_create(size_t bytes, void** buffer, void* ipc_handle_64);
+
+/* Maps a peer's buffer from its handle (peer access is enabled on demand). */
+int lq2_allreduce_buffer_open(const void* ipc_handle_64, void** buffer);
+
+/* Unmaps a peer's buffer (own == 0) or frees this rank's (own != 0). */
+int lq2_allreduce_buffer_close(void* buffer, int own);
+
+/*
+ * out[i] = sum over ranks of x[i], i < count (fp16; count * 2 a multiple of 16 and at most
+ * max_message_bytes, else LQ2_ERR_SHAPE / LQ2_ERR_LIMIT).  out may alias x.
+ * buffers: host array of `world` device pointers (this rank's own buffer at index rank).
+ * Waits inside the kernel are bounded; a peer that never arrives is counted in
+ * lq2_allreduce_timeouts() instead of hanging the GPU (the output is then invalid).
+ */
+int lq2_allreduce_fp16(const void* x, void* out, int64_t count, void* const* buffers, int rank, int world,
+                       size_t max_message_bytes, void* stream);
+
+/*
+ * The all-reduce above followed by the residual RMSNorm of lq2_rmsnorm, in one launch:
+ *   h = fp16(sum over ranks of x);  s = fp32(h) + fp32(residual);  residual_out = fp16(s);
+ *   out = fp16(s * rsqrt(mean(s^2) + eps)) * weight
+ * i.e. tp.all_reduce(o_proj(...)) / tp.all_reduce(down_proj(...)) and the layer norm that
+ * consumes it (qslab/runtime/model/qwen3.py:53,64 with primitives.py:23-30).  x [rows, hidden]
+ * is this rank's partial sum (row stride x_row_stride); rows * hidden * 2 must not exceed
+ * max_message_bytes (LQ2_ERR_LIMIT).  Counts as one call in the sequence all ranks share.
+ */
+int lq2_rmsnorm_allreduce(const void* x, int64_t x_row_stride, const void* residual, const void* weight, void* out,
+                          void* residual_out, int rows, int hidden, float eps, void* const* buffers, int rank,
+                          int world, size_t max_message_bytes, void* stream);
+
+/* Number of abandoned waits on the current device since the library was loaded
+ * (synchronises the device); 0 in a healthy run. */
+unsigned int lq2_allreduce_timeouts(void);
+
 #ifdef __cplusplus
 }
 #endif

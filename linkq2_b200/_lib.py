@@ -7,7 +7,7 @@ else.  Build it with ``python -m linkq2_b200.build``.
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
+from ctypes import c_char_p, c_float, c_int, c_int64, c_size_t, c_uint, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "liblinkq2_b200.so"
@@ -21,6 +21,14 @@ SIGNATURES = {
     "lq2_abi_version": (c_int, []),
     "lq2_w4_pack": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p]),
     "lq2_w4a16_set_constant_weights": (c_int, [c_int]),
+    "lq2_allreduce_buffer_bytes": (c_size_t, [c_int, c_size_t]),
+    "lq2_allreduce_buffer_create": (c_int, [c_size_t, c_void_p, c_void_p]),
+    "lq2_allreduce_buffer_open": (c_int, [c_void_p, c_void_p]),
+    "lq2_allreduce_buffer_close": (c_int, [c_void_p, c_int]),
+    "lq2_allreduce_fp16": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int, c_size_t, c_void_p]),
+    "lq2_rmsnorm_allreduce": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                      c_float, c_void_p, c_int, c_int, c_size_t, c_void_p]),
+    "lq2_allreduce_timeouts": (c_uint, []),
     "lq2_w4a16_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "lq2_w4a16_linear": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),

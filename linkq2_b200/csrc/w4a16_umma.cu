@@ -34,6 +34,9 @@
 // All waits are bounded (see mbar_wait_bounded).
 #include <cooperative_groups.h>
 #include <cuda.h>
+#ifdef LQ2_TUNING
+#include <cstdlib>
+#endif
 
 #include "common.cuh"
 
@@ -44,9 +47,10 @@ namespace lq2 {
 namespace {
 
 constexpr int kUM = 128;          // output channels per CTA (MMA M)
-// k per pipeline stage (64 or 128)
+// k per pipeline stage: 128 for batch tiles up to 64 rows (half as many barrier rounds per
+// byte as 64, measured 8-15 % faster), 64 beyond, where the activation tile of a stage grows
 #ifndef LQ2_UMMA_SMALL_STAGE_K
-#define LQ2_UMMA_SMALL_STAGE_K 64
+#define LQ2_UMMA_SMALL_STAGE_K 128
 #endif
 __host__ __device__ constexpr int stage_k(int mb) { return mb <= 64 ? LQ2_UMMA_SMALL_STAGE_K : 64; }
 constexpr int kUThreads = 320;    // 10 warps
@@ -160,7 +164,14 @@ __host__ __device__ constexpr uint32_t umma_idesc(int mma_m, int mma_n) {
 template <int MB, int GPSU>
 struct ULayout {
     static constexpr int UK = stage_k(MB);
-    static constexpr int A_STAGES = 3;
+    // A tiles in tensor memory.  A 128-k tile takes 64 columns; one of them plus the accumulator
+    // fits the 128-column allocation that lets four CTAs share an SM, and the MMAs of a stage
+    // are short enough that the next stage's conversion (in registers) hides them.
+#ifdef LQ2_U_ASTAGES
+    static constexpr int A_STAGES = LQ2_U_ASTAGES;
+#else
+    static constexpr int A_STAGES = UK == 128 ? 1 : 3;
+#endif
     static constexpr int A_COLS = UK / 2;                           // 32-bit TMEM columns per A tile (two fp16 each)
     static constexpr int XBOX_BYTES = (MB * 128 + 1023) / 1024 * 1024;   // [MB m][64 k] fp16, swizzled
     static constexpr int X_BYTES = (UK / 64) * XBOX_BYTES;
@@ -168,7 +179,11 @@ struct ULayout {
     static constexpr int S_BYTES = GPSU * kUM * 2;                  // [GPSU][128 n] fp16
     static constexpr int RAW_OFF = X_BYTES, S_OFF = RAW_OFF + RAW_BYTES, Z_OFF = S_OFF + S_BYTES;
     static constexpr int R_STAGE_BYTES = (Z_OFF + S_BYTES + 1023) / 1024 * 1024;   // x tile first: 1 KiB aligned
+#ifdef LQ2_U_RSTAGES
+    static constexpr int R_STAGES = LQ2_U_RSTAGES;
+#else
     static constexpr int R_STAGES = UK == 128 ? (MB <= 16 ? 4 : 3) : (MB <= 64 ? 6 : (MB <= 128 ? 4 : 3));
+#endif
     static constexpr int TX_BYTES = (UK / 64) * MB * 128 + RAW_BYTES;   // + S_BYTES (x2 with zero points)
     static constexpr int R_RING_OFF = 0;
     static constexpr int RING_BYTES = R_RING_OFF + R_STAGES * R_STAGE_BYTES;
@@ -183,12 +198,26 @@ struct ULayout {
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
+#ifdef LQ2_U_TIMELINE
+__device__ unsigned long long g_timeline[8 * 4096];
+__device__ __forceinline__ void stamp(int slot) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (cta < 4096) g_timeline[cta * 8 + slot] = t;
+}
+#define LQ2_STAMP(slot, cond) do { if (cond) stamp(slot); } while (0)
+#else
+#define LQ2_STAMP(slot, cond) do { } while (0)
+#endif
+
 template <int MB, bool ZTABLE, int GPSU>
 __global__ void __launch_bounds__(kUThreads, 1)
 w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                   const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                   const UParams p) {
     using L = ULayout<MB, GPSU>;
+    LQ2_STAMP(0, threadIdx.x == 0);                                    // entry
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int RS = L::R_STAGES, AS = L::A_STAGES, UK = L::UK;
@@ -233,6 +262,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     // before the allocation above, its CTAs could take the tensor memory this one still needs and then
     // wait for this grid to finish.
     pdl_launch_dependents();
+    LQ2_STAMP(1, threadIdx.x == 0);                                    // prologue done
     const uint32_t tmem_base = *tmem_slot;
     unsigned char* r_ring = smem + L::R_RING_OFF;
 
@@ -262,6 +292,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
         if (lane == 0)
             for (int it = 0; it < ahead; ++it) load_weights(it);
         if (p.early_weights) pdl_wait();
+        LQ2_STAMP(2, lane == 0);                                       // previous grid complete
         if (lane == 0)
             for (int it = 0; it < ahead; ++it) load_activations(it);
         __syncwarp();
@@ -284,6 +315,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             if (lane == 0) {
                 const uint32_t a_tmem = tmem_base + L::ACC_COLS + aslot * L::A_COLS;
                 const uint32_t xbase = smem_u32(r_ring + rslot * L::R_STAGE_BYTES);
+#ifndef LQ2_U_SKIP_MMA
 #pragma unroll
                 for (int kk = 0; kk < UK / 16; ++kk) {
                     // a K step of 16 fp16: 8 TMEM columns of A, 32 bytes inside the swizzled rows of B
@@ -292,6 +324,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                                 smem_desc_sw128(xbase + (kk >> 2) * L::XBOX_BYTES + (kk & 3) * 32), idesc,
                                 (it > 0 || kk > 0) ? 1u : 0u);
                 }
+#endif
                 umma_commit(a_free(aslot));                   // both buffers are reusable once these MMAs are done
                 umma_commit(raw_free(rslot));
                 if (it == my_stages - 1) umma_commit(acc_full);
@@ -321,6 +354,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             const int rslot = it % RS, aslot = it % AS;
             const unsigned char* rbase = r_ring + rslot * L::R_STAGE_BYTES;
             mbar_wait_bounded(raw_full(rslot), (it / RS) & 1);
+            LQ2_STAMP(3, it == 0 && warp == 2 && lane == 0);           // first stage landed
             const uint32_t* raw = reinterpret_cast<const uint32_t*>(rbase + L::RAW_OFF);
             const __half* sc = reinterpret_cast<const __half*>(rbase + L::S_OFF);
             const __half* zc = reinterpret_cast<const __half*>(rbase + L::Z_OFF);
@@ -359,6 +393,16 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                     cols[4 * r4 + 1] = __byte_perm(v26, v37, 0x5410);        // k2 k3
                     cols[4 * r4 + 2] = __byte_perm(v04, v15, 0x7632);        // k4 k5
                     cols[4 * r4 + 3] = __byte_perm(v26, v37, 0x7632);        // k6 k7
+#ifdef LQ2_U_SKIP_ALU
+                    cols[4 * r4 + 0] = w; cols[4 * r4 + 1] = w8; cols[4 * r4 + 2] = w; cols[4 * r4 + 3] = w8;
+#endif
+#ifdef LQ2_U_SUBNORMAL_PROBE
+                    // raw codes as fp16 subnormals u * 2^-24, natural k order, no scale, no zero point
+                    cols[4 * r4 + 0] = (w & 0xfu) | ((w & 0xf0u) << 12);
+                    cols[4 * r4 + 1] = ((w >> 8) & 0xfu) | (((w >> 8) & 0xf0u) << 12);
+                    cols[4 * r4 + 2] = ((w >> 16) & 0xfu) | (((w >> 16) & 0xf0u) << 12);
+                    cols[4 * r4 + 3] = ((w >> 24) & 0xfu) | (((w >> 24) & 0xf0u) << 12);
+#endif
                 }
                 tmem_st16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + aslot * L::A_COLS +
                               khalf * (UK / 4) + 16 * b, cols);
@@ -375,6 +419,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             mbar_wait_bounded(acc_full, 0);
             tc_fence_after();
         }
+        LQ2_STAMP(4, warp == 2 && lane == 0);                          // all MMAs done
     }
     __syncthreads();                                       // the ring is idle from here on
     if (warp >= 2 && warp < 6) {
@@ -397,6 +442,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem_base, L::TMEM_COLS);
     if (ranks > 1) cluster.sync();
+    LQ2_STAMP(5, threadIdx.x == 0);                                    // partials visible in the cluster
     {
         constexpr int QUADS = kUM / 4;
         const int q0 = rank * QUADS / ranks, q1 = (rank + 1) * QUADS / ranks;
@@ -417,7 +463,9 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             }
         }
     }
+    LQ2_STAMP(6, threadIdx.x == 0);                                    // output written
     if (ranks > 1) cluster.sync();
+    LQ2_STAMP(7, threadIdx.x == 0);                                    // exit
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -465,6 +513,9 @@ UPlan make_uplan(int m, int n, int k) {
     int r = 1;
     const int resident = kNumSMs * (p.mb <= 32 ? 3 : (p.mb <= 128 ? 2 : 1));
     while (r < 8 && base * r * 2 <= resident && stages / (r * 2) >= 4) r *= 2;
+#ifdef LQ2_TUNING
+    if (const char* e = getenv("LQ2_U_RANKS")) r = atoi(e);
+#endif
     p.ranks = r;
     p.spr = cdiv(stages, r);
     return p;

@@ -39,6 +39,31 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.T
     return out if residual is None else (out, res_out.view(x.shape))
 
 
+def rmsnorm_allreduce(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor, exchange):
+    """``rmsnorm(all_reduce(x), weight, eps, residual)`` in one launch: ``x`` is this
+    rank's partial sum; the exchange runs over peer memory inside the norm kernel
+    (``exchange``: the ``PeerExchange`` of the tensor-parallel group).  Returns
+    ``(normalised, all_reduce(x) + residual)``."""
+    if x.dtype != torch.float16 or not x.is_cuda:
+        raise TypeError("rmsnorm_allreduce runs on CUDA fp16 tensors")
+    hidden = x.shape[-1]
+    x2 = x.reshape(-1, hidden)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    rows = x2.shape[0]
+    res_in = residual.reshape(-1, hidden)
+    res_in = res_in if res_in.is_contiguous() else res_in.contiguous()
+    out = torch.empty((rows, hidden), dtype=torch.float16, device=x.device)
+    res_out = torch.empty_like(out)
+    with torch.cuda.device(x.device):
+        status = _lib.lib.lq2_rmsnorm_allreduce(
+            x2.data_ptr(), x2.stride(0), res_in.data_ptr(), weight.data_ptr(), out.data_ptr(), res_out.data_ptr(),
+            rows, hidden, eps, exchange.table, exchange.rank, exchange.world, exchange.max_bytes, _stream(x))
+    _lib.check(status, "lq2_rmsnorm_allreduce")
+    _lib.count()
+    return out.view(x.shape), res_out.view(x.shape)
+
+
 def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` for ``[rows, width] fp16`` tensors (row strides allowed)."""
     if gate.dtype != torch.float16 or not gate.is_cuda:

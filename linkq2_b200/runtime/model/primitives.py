@@ -15,8 +15,13 @@ class RMSNorm(nn.Module):
         self.eps = eps
         self.weight = nn.Parameter(torch.ones(hidden_size), requires_grad=False)
 
-    def forward(self, x, residual=None):
-        from linkq2_b200.kernels.fused import rmsnorm
+    def forward(self, x, residual=None, deferred=False):
+        """``deferred``: ``x`` is this rank's partial sum of a row-split projection;
+        the tensor-parallel all-reduce is done inside the norm kernel."""
+        from linkq2_b200.kernels.fused import rmsnorm, rmsnorm_allreduce
+        if deferred:
+            from linkq2_b200.runtime.parallel import get_tp
+            return rmsnorm_allreduce(x, self.weight, self.eps, residual, get_tp().exchange)
         return rmsnorm(x, self.weight, self.eps, residual)
 
     def reference_forward(self, x, residual=None):

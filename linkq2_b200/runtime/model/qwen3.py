@@ -114,7 +114,7 @@ class Qwen3Attention(nn.Module):
                              slot_mapping=ctx.slot_mapping if store else None, v_group=attn.v_group,
                              want_k=ctx.is_prefill)
         o = attn.attend(q, k, v)
-        return self.tp.all_reduce(self.o_proj(o.flatten(1, -1)))
+        return self.tp.reduce_or_defer(self.o_proj(o.flatten(1, -1)))
 
 
 class Qwen3MLP(nn.Module):
@@ -139,7 +139,7 @@ class Qwen3MLP(nn.Module):
             gate, up = self.gate_up_proj(x).chunk(2, dim=-1)
         else:
             gate, up = self.gate_proj(x), self.up_proj(x)
-        return self.tp.all_reduce(self.down_proj(silu_mul(gate, up)))
+        return self.tp.reduce_or_defer(self.down_proj(silu_mul(gate, up)))
 
 
 class Qwen3DecoderLayer(nn.Module):
@@ -150,14 +150,18 @@ class Qwen3DecoderLayer(nn.Module):
         self.input_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
         self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
 
-    def forward(self, positions, hidden_states, residual):
+    def forward(self, positions, hidden_states, residual, deferred=False):
+        """``deferred``: ``hidden_states`` is the previous layer's MLP output before its
+        tensor-parallel all-reduce, which the norm below then performs itself.  Returns
+        ``(mlp_out, residual, deferred)`` in the same convention."""
         if residual is None:
             hidden_states, residual = self.input_layernorm(hidden_states), hidden_states
         else:
-            hidden_states, residual = self.input_layernorm(hidden_states, residual)
-        hidden_states = self.self_attn(positions, hidden_states)
-        hidden_states, residual = self.post_attention_layernorm(hidden_states, residual)
-        return self.mlp(hidden_states), residual
+            hidden_states, residual = self.input_layernorm(hidden_states, residual, deferred=deferred)
+        hidden_states, deferred = self.self_attn(positions, hidden_states)
+        hidden_states, residual = self.post_attention_layernorm(hidden_states, residual, deferred=deferred)
+        hidden_states, deferred = self.mlp(hidden_states)
+        return hidden_states, residual, deferred
 
 
 class Qwen3Model(nn.Module):
@@ -170,10 +174,10 @@ class Qwen3Model(nn.Module):
         self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
 
     def forward(self, input_ids, positions):
-        hidden_states, residual = self.embed_tokens(input_ids), None
+        hidden_states, residual, deferred = self.embed_tokens(input_ids), None, False
         for layer in self.layers:
-            hidden_states, residual = layer(positions, hidden_states, residual)
-        hidden_states, _ = self.norm(hidden_states, residual)
+            hidden_states, residual, deferred = layer(positions, hidden_states, residual, deferred)
+        hidden_states, _ = self.norm(hidden_states, residual, deferred=deferred)
         return hidden_states
 
 

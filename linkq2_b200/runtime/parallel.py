@@ -17,16 +17,106 @@ import torch
 import torch.distributed as dist
 
 
+class PeerExchange:
+    """The exchange buffers of ``lq2_allreduce_fp16``: this rank's buffer (allocated
+    by the library, shared through CUDA IPC) and the mapped buffers of its peers.
+
+    Built collectively by ``create``; if any rank cannot allocate, export or map a
+    buffer (no peer access, IPC unavailable), every rank gets ``None`` and the
+    all-reduce stays on NCCL."""
+
+    def __init__(self, rank, world, max_bytes, own, table, pointers):
+        self.rank, self.world, self.max_bytes = rank, world, max_bytes
+        self._own, self.table, self._pointers = own, table, pointers
+
+    @classmethod
+    def create(cls, rank: int, world: int, device, max_bytes: int, group=None) -> "PeerExchange | None":
+        import ctypes
+        from linkq2_b200 import _lib
+        lib = _lib.lib
+        pointers, own, ok = [None] * world, ctypes.c_void_p(), True
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(device):
+            size = lib.lq2_allreduce_buffer_bytes(world, max_bytes)
+            ok = size > 0 and lib.lq2_allreduce_buffer_create(size, ctypes.byref(own), handle) == _lib.OK
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle.raw) if ok else None, group=group)
+            ok = ok and all(h is not None for h in handles)
+            if ok:
+                for peer in range(world):
+                    if peer == rank:
+                        pointers[peer] = own.value
+                        continue
+                    mapped = ctypes.c_void_p()
+                    if lib.lq2_allreduce_buffer_open(handles[peer], ctypes.byref(mapped)) != _lib.OK:
+                        ok = False
+                        break
+                    pointers[peer] = mapped.value
+            agreed = [None] * world
+            dist.all_gather_object(agreed, bool(ok), group=group)
+            if not all(agreed):
+                for peer, ptr in enumerate(pointers):
+                    if ptr and peer != rank:
+                        lib.lq2_allreduce_buffer_close(ptr, 0)
+                if own.value:
+                    lib.lq2_allreduce_buffer_close(own.value, 1)
+                return None
+        table = (ctypes.c_void_p * world)(*pointers)
+        return cls(rank, world, max_bytes, own.value, table, pointers)
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        from linkq2_b200 import _lib
+        with torch.cuda.device(x.device):
+            status = _lib.lib.lq2_allreduce_fp16(x.data_ptr(), x.data_ptr(), x.numel(), self.table, self.rank,
+                                                 self.world, self.max_bytes,
+                                                 torch.cuda.current_stream().cuda_stream)
+        _lib.check(status, "lq2_allreduce_fp16")
+        _lib.count()
+        return x
+
+    def accepts(self, x: torch.Tensor) -> bool:
+        nbytes = x.numel() * x.element_size()
+        return (x.dtype == torch.float16 and x.is_cuda and x.is_contiguous() and 0 < nbytes <= self.max_bytes
+                and nbytes % 16 == 0 and x.data_ptr() % 16 == 0)
+
+    def timeouts(self) -> int:
+        from linkq2_b200 import _lib
+        return int(_lib.lib.lq2_allreduce_timeouts())
+
+    def close(self):
+        from linkq2_b200 import _lib
+        for peer, ptr in enumerate(self._pointers):
+            if ptr and peer != self.rank:
+                _lib.lib.lq2_allreduce_buffer_close(ptr, 0)
+        if self._own:
+            _lib.lib.lq2_allreduce_buffer_close(self._own, 1)
+        self._pointers, self._own = [], None
+
+
 @dataclass
 class TensorParallel:
     rank: int = 0
     size: int = 1
     group: object | None = None
+    exchange: PeerExchange | None = None
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        """Sum over the ranks, in place.  Small fp16 activations go through the
+        library's peer-memory kernel, everything else through NCCL / gloo."""
         if self.size > 1:
+            if self.exchange is not None and self.exchange.accepts(x):
+                return self.exchange.all_reduce(x)
             dist.all_reduce(x, op=dist.ReduceOp.SUM, group=self.group)
         return x
+
+    def reduce_or_defer(self, x: torch.Tensor):
+        """``(tensor, deferred)``: a partial sum that the next residual RMSNorm can
+        reduce itself (``rmsnorm_allreduce``) is handed on unreduced with ``deferred``
+        set; otherwise it is all-reduced here.  The decision depends on shape and
+        dtype only, so all ranks take it alike."""
+        if self.size > 1 and self.exchange is not None and self.exchange.accepts(x):
+            return x, True
+        return self.all_reduce(x), False
 
     def check_geometry(self, hidden, intermediate, num_heads, num_kv_heads, group_size):
         t = self.size
@@ -50,9 +140,12 @@ def set_tp(tp: TensorParallel) -> None:
     _TP = tp
 
 
-def init_from_env(backend: str | None = None) -> TensorParallel:
+def init_from_env(backend: str | None = None, peer_exchange_bytes: int = 4 << 20) -> TensorParallel:
     """Join the process group described by RANK / WORLD_SIZE / MASTER_* and make
-    the whole world one tensor-parallel group."""
+    the whole world one tensor-parallel group.  On NCCL, all-reduces of fp16
+    activations of up to ``peer_exchange_bytes`` (decode and verify steps) use the
+    library's own kernel over peer memory when the GPUs can map each other's
+    memory; ``LQ2_PEER_ALLREDUCE=0`` keeps everything on NCCL."""
     import os
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world == 1:
@@ -64,7 +157,12 @@ def init_from_env(backend: str | None = None) -> TensorParallel:
         if backend == "nccl":
             kwargs["device_id"] = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         dist.init_process_group(backend=backend, **kwargs)
-    set_tp(TensorParallel(dist.get_rank(), dist.get_world_size(), None))
+    tp = TensorParallel(dist.get_rank(), dist.get_world_size(), None)
+    if (dist.get_backend() == "nccl" and tp.size <= 8 and peer_exchange_bytes > 0
+            and os.environ.get("LQ2_PEER_ALLREDUCE", "1") != "0"):
+        device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        tp.exchange = PeerExchange.create(tp.rank, tp.size, device, peer_exchange_bytes)
+    set_tp(tp)
     return get_tp()
 
 
@@ -76,6 +174,9 @@ def shutdown():
         if torch.cuda.is_available():
             torch.cuda.synchronize()
         dist.barrier()
+        if get_tp().exchange is not None:
+            get_tp().exchange.close()
+            dist.barrier()
         dist.destroy_process_group()
     set_tp(TensorParallel())
 

@@ -41,6 +41,92 @@ def _worker(rank, world, port, ckpt, prompts, eager, results):
     parallel.shutdown()
 
 
+def _exchange_worker(rank, world, port, results):
+    """The library's peer-memory all-reduce against a rank-ordered fp32 sum of the
+    all-gathered addends (bit-exact), eagerly and replayed from a CUDA graph."""
+    import torch.distributed as dist
+    from linkq2_b200.runtime import parallel
+    os.environ.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    tp = parallel.init_from_env("nccl")
+    if tp.exchange is None:
+        results[rank] = "unavailable"
+        parallel.shutdown()
+        return
+    g = torch.Generator().manual_seed(100 + rank)
+
+    def expected_sum(x):
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x)
+        acc = torch.zeros_like(x, dtype=torch.float32)
+        for part in parts:                      # rank order, fp32, one rounding at the end
+            acc += part.float()
+        return acc.half()
+
+    checked = 0
+    for shape in [(1, 4096), (32, 4096), (3, 8), (512, 1024), (17, 2048), (32, 4096)]:
+        for _ in range(3):                      # consecutive calls alternate the buffer halves
+            x = (torch.randn(*shape, generator=g) * (1 + rank)).half().cuda()
+            want = expected_sum(x)
+            assert tp.exchange.accepts(x)
+            got = tp.all_reduce(x.clone())
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), (shape, (got.float() - want.float()).abs().max())
+            checked += 1
+    # the same exchange inside the residual RMSNorm kernel
+    from linkq2_b200.kernels.fused import rmsnorm, rmsnorm_allreduce
+    for rows, hidden in [(1, 4096), (32, 4096), (5, 1024), (64, 8192), (32, 4096)]:
+        for _ in range(2):
+            x = (torch.randn(rows, hidden, generator=g) * (1 + rank)).half().cuda()
+            res = torch.randn(rows, hidden, generator=torch.Generator().manual_seed(rows + hidden)).half().cuda()
+            w = (1 + 0.1 * torch.randn(hidden, generator=torch.Generator().manual_seed(hidden))).half().cuda()
+            want_out, want_res = rmsnorm(expected_sum(x), w, 1e-6, res)
+            got_out, got_res = rmsnorm_allreduce(x, w, 1e-6, res, tp.exchange)
+            torch.cuda.synchronize()
+            assert torch.equal(got_res, want_res) and torch.equal(got_out, want_out), (rows, hidden)
+            checked += 1
+    big = torch.ones(2048, 4096, dtype=torch.float16, device="cuda")           # above the limit: NCCL
+    assert not tp.exchange.accepts(big)
+    assert torch.equal(tp.all_reduce(big), torch.full_like(big, world))
+    # a chain of dependent all-reduces inside a CUDA graph
+    a = (torch.randn(32, 4096, generator=g)).half().cuda()
+    side = torch.cuda.Stream()
+
+    def chain():
+        y = tp.all_reduce(a * 0.5)
+        z = tp.all_reduce(y * 0.25 + a)
+        return tp.all_reduce(z * 0.125)
+    with torch.cuda.stream(side):
+        eager = chain()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            out = chain()
+        for _ in range(4):
+            out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, eager)
+    assert tp.exchange.timeouts() == 0
+    del graph
+    results[rank] = checked
+    parallel.shutdown()
+
+
+def test_peer_memory_all_reduce_is_bit_exact():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world, port = 2, _free_port()
+    with mp.Manager() as manager:
+        results = manager.dict()
+        mp.spawn(_exchange_worker, args=(world, port, results), nprocs=world, join=True)
+        results = dict(results)
+    if any(v == "unavailable" for v in results.values()):
+        pytest.skip("CUDA IPC / peer access is not available between these GPUs")
+    assert results == {0: 28, 1: 28}
+
+
 @pytest.mark.parametrize("eager", [True, False])
 def test_two_gpu_tokens_match_oracle(tmp_path, eager):
     if torch.cuda.device_count() < 2:

@@ -474,6 +474,10 @@ int launch_one(const W4Params& p, const Plan& pl, cudaStream_t st) {
     if (!configured[dev]) {
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES) != cudaSuccess)
             return LQ2_ERR_CUDA;
+        // several CTAs per SM are planned for: ask for the largest shared-memory carve-out
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+            return LQ2_ERR_CUDA;
         configured[dev] = true;
     }
     alignas(64) CUtensorMap map_w, map_x, map_s, map_z;

@@ -37,6 +37,7 @@
 #ifdef LQ2_TUNING
 #include <cstdlib>
 #endif
+#include <algorithm>
 
 #include "common.cuh"
 
@@ -46,6 +47,7 @@ namespace lq2 {
 
 namespace {
 
+constexpr int kMaxSmemPerCta = 227 * 1024;
 constexpr int kUM = 128;          // output channels per CTA (MMA M)
 // k per pipeline stage: 128 for batch tiles up to 64 rows (half as many barrier rounds per
 // byte as 64, measured 8-15 % faster), 64 beyond, where the activation tile of a stage grows
@@ -97,6 +99,10 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
         ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(bar) : "memory");
 }
+
+// ---- cluster barrier, split into its two halves
+__device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory"); }
 
 // ---- tcgen05 wrappers (cta_group::1)
 __device__ __forceinline__ void tmem_alloc(uint32_t smem_dst, uint32_t ncols) {
@@ -188,7 +194,13 @@ struct ULayout {
     static constexpr int R_RING_OFF = 0;
     static constexpr int RING_BYTES = R_RING_OFF + R_STAGES * R_STAGE_BYTES;
     static constexpr int RED_BYTES = MB * kUM * 4;
-    static constexpr int DATA_BYTES = RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES;
+    // Split-K reduction.  Up to 64 batch rows every CTA has a receive area of its own
+    // ([source rank][MB][128 / ranks] fp32, never aliased with the ring) into which the
+    // ranks of its cluster push their partial sums; beyond, the partial tile is staged
+    // in the idle ring and pulled by the owners of the column slices.
+    static constexpr bool PUSH = MB <= 64;
+    static constexpr int RECV_OFF = RING_BYTES;
+    static constexpr int DATA_BYTES = PUSH ? RING_BYTES + RED_BYTES : (RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES);
     static constexpr int NBARS = 2 * R_STAGES + 2 * A_STAGES + 1;
     static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + NBARS * 8 + 16;
     static constexpr int ACC_COLS = MB < 32 ? 32 : MB;
@@ -211,8 +223,12 @@ __device__ __forceinline__ void stamp(int slot) {
 #define LQ2_STAMP(slot, cond) do { } while (0)
 #endif
 
+// CTAs per SM the plan counts on (shared memory and tensor-memory columns allow them; the
+// launch bounds make the register allocation follow)
+__host__ __device__ constexpr int resident_ctas(int mb) { return mb <= 32 ? 3 : (mb <= 64 ? 2 : 1); }
+
 template <int MB, bool ZTABLE, int GPSU>
-__global__ void __launch_bounds__(kUThreads, 1)
+__global__ void __launch_bounds__(kUThreads, resident_ctas(MB))
 w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                   const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                   const UParams p) {
@@ -262,6 +278,9 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     // before the allocation above, its CTAs could take the tensor memory this one still needs and then
     // wait for this grid to finish.
     pdl_launch_dependents();
+    // first half of a cluster barrier: by the time the epilogue waits for it, every CTA of
+    // the cluster is known to be running, which remote shared-memory stores require
+    if (L::PUSH && ranks > 1) cluster_arrive_release();
     LQ2_STAMP(1, threadIdx.x == 0);                                    // prologue done
     const uint32_t tmem_base = *tmem_slot;
     unsigned char* r_ring = smem + L::R_RING_OFF;
@@ -413,7 +432,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
 
     // ---- epilogue: warps 2-5 read the accumulator (TMEM lane = output channel)
     cg::cluster_group cluster = cg::this_cluster();
-    float* red = reinterpret_cast<float*>(smem);          // [MB][128]
     if (warp >= 2 && warp < 6) {
         if (my_stages > 0) {
             mbar_wait_bounded(acc_full, 0);
@@ -421,51 +439,106 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
         }
         LQ2_STAMP(4, warp == 2 && lane == 0);                          // all MMAs done
     }
-    __syncthreads();                                       // the ring is idle from here on
-    if (warp >= 2 && warp < 6) {
-        const int quarter = warp & 3;                      // TMEM lanes 32*quarter .. +31 belong to this warp
-        const int nl = quarter * 32 + lane;
+    if constexpr (L::PUSH) {
+        // Push: rank q of the cluster owns channels [q * W, (q + 1) * W) of the tile.  Every rank
+        // writes its partial sums for those channels straight from registers into q's receive
+        // area (remote shared memory), one cluster barrier follows, and q adds the ranks' parts
+        // in rank order.  Nobody reads remote memory after the barrier, so a CTA may leave as
+        // soon as it has written its slice.
+        const int W = kUM / ranks;
+        float* recv = reinterpret_cast<float*>(smem + L::RECV_OFF);   // [ranks][MB][W]
+        if (ranks > 1) cluster_wait_acquire();                        // all CTAs of the cluster are running
+        if (warp >= 2 && warp < 6) {
+            const int quarter = warp & 3;                  // TMEM lanes 32*quarter .. +31 belong to this warp
+            const int nl = quarter * 32 + lane;
+            const int dest = nl / W, c = nl - dest * W;
+            float* dst = (ranks > 1 ? cluster.map_shared_rank(recv, dest) : recv) + size_t(rank) * MB * W + c;
+#pragma unroll 1
+            for (int c0 = 0; c0 < MB; c0 += 16) {
+                float v[16];
+                if (my_stages > 0) {
+                    tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + c0, v);
+                } else {
 #pragma unroll
-        for (int c0 = 0; c0 < MB; c0 += 16) {
-            float v[16];
-            if (my_stages > 0) {
-                tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + c0, v);
-            } else {
+                    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+                }
 #pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] = 0.f;
+                for (int i = 0; i < 16; ++i) dst[(c0 + i) * W] = v[i];
             }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) red[(c0 + i) * kUM + nl] = v[i];
         }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem_base, L::TMEM_COLS);
-    if (ranks > 1) cluster.sync();
-    LQ2_STAMP(5, threadIdx.x == 0);                                    // partials visible in the cluster
-    {
-        constexpr int QUADS = kUM / 4;
-        const int q0 = rank * QUADS / ranks, q1 = (rank + 1) * QUADS / ranks;
-        const int quads = q1 - q0;
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 1) tmem_dealloc(tmem_base, L::TMEM_COLS);
+        if (ranks > 1) {
+            cluster_arrive_release();
+            cluster_wait_acquire();
+        }
+        LQ2_STAMP(5, threadIdx.x == 0);                                // all parts of my slice have arrived
+        const int quads = W / 4;
         for (int e = tid; e < rows * quads; e += kUThreads) {
-            const int ml = e / quads, col = (q0 + e % quads) * 4;
+            const int ml = e / quads, col = (e - ml * quads) * 4;
             float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int q = 0; q < ranks; ++q) {
-                const float* src = ranks > 1 ? cluster.map_shared_rank(red, q) : red;
-                const float4 v = *reinterpret_cast<const float4*>(src + ml * kUM + col);
+                const float4 v = *reinterpret_cast<const float4*>(recv + (size_t(q) * MB + ml) * W + col);
                 sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
             }
-            const int nn = tile_n0 + col;
+            const int nn = tile_n0 + rank * W + col;
             if (nn < p.n) {
                 const __half2 lo = __floats2half2_rn(sum.x, sum.y);
                 const __half2 hi = __floats2half2_rn(sum.z, sum.w);
                 *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * p.n + nn) = make_uint2(h2_as_u32(lo), h2_as_u32(hi));
             }
         }
+        LQ2_STAMP(6, threadIdx.x == 0);                                // output written
+        LQ2_STAMP(7, threadIdx.x == 0);
+    } else {
+        float* red = reinterpret_cast<float*>(smem);          // [MB][128], in the idle ring
+        __syncthreads();                                       // the ring is idle from here on
+        if (warp >= 2 && warp < 6) {
+            const int quarter = warp & 3;
+            const int nl = quarter * 32 + lane;
+#pragma unroll
+            for (int c0 = 0; c0 < MB; c0 += 16) {
+                float v[16];
+                if (my_stages > 0) {
+                    tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + c0, v);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) red[(c0 + i) * kUM + nl] = v[i];
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 1) tmem_dealloc(tmem_base, L::TMEM_COLS);
+        if (ranks > 1) cluster.sync();
+        LQ2_STAMP(5, threadIdx.x == 0);                                // partials visible in the cluster
+        {
+            constexpr int QUADS = kUM / 4;
+            const int q0 = rank * QUADS / ranks, q1 = (rank + 1) * QUADS / ranks;
+            const int quads = q1 - q0;
+            for (int e = tid; e < rows * quads; e += kUThreads) {
+                const int ml = e / quads, col = (q0 + e % quads) * 4;
+                float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int q = 0; q < ranks; ++q) {
+                    const float* src = ranks > 1 ? cluster.map_shared_rank(red, q) : red;
+                    const float4 v = *reinterpret_cast<const float4*>(src + ml * kUM + col);
+                    sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+                }
+                const int nn = tile_n0 + col;
+                if (nn < p.n) {
+                    const __half2 lo = __floats2half2_rn(sum.x, sum.y);
+                    const __half2 hi = __floats2half2_rn(sum.z, sum.w);
+                    *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * p.n + nn) = make_uint2(h2_as_u32(lo), h2_as_u32(hi));
+                }
+            }
+        }
+        LQ2_STAMP(6, threadIdx.x == 0);                                // output written
+        if (ranks > 1) cluster.sync();                                 // nobody leaves while its tile is still being read
+        LQ2_STAMP(7, threadIdx.x == 0);                                // exit
     }
-    LQ2_STAMP(6, threadIdx.x == 0);                                    // output written
-    if (ranks > 1) cluster.sync();
-    LQ2_STAMP(7, threadIdx.x == 0);                                    // exit
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -511,7 +584,7 @@ UPlan make_uplan(int m, int n, int k) {
     const int stages = cdiv(k, stage_k(p.mb));
     const int base = p.n_tiles * p.m_tiles;
     int r = 1;
-    const int resident = kNumSMs * (p.mb <= 32 ? 3 : (p.mb <= 128 ? 2 : 1));
+    const int resident = kNumSMs * resident_ctas(p.mb);
     while (r < 8 && base * r * 2 <= resident && stages / (r * 2) >= 4) r *= 2;
 #ifdef LQ2_TUNING
     if (const char* e = getenv("LQ2_U_RANKS")) r = atoi(e);
@@ -530,7 +603,11 @@ int launch_umma(const __half* x, int64_t ldx, const int32_t* packed, const __hal
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LQ2_ERR_CUDA;
     if (!configured[dev]) {
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES) != cudaSuccess)
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemPerCta) != cudaSuccess)
+            return LQ2_ERR_CUDA;
+        // several CTAs per SM are planned for: ask for the largest shared-memory carve-out
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return LQ2_ERR_CUDA;
         configured[dev] = true;
     }
@@ -541,7 +618,17 @@ int launch_umma(const __half* x, int64_t ldx, const int32_t* packed, const __hal
     ok = ok && make_map(&map_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales, n, groups, n * 2, kUM, GPSU, false);
     ok = ok && make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ZTABLE ? zeros : scales, n, groups, n * 2, kUM, GPSU, false);
     if (!ok) return LQ2_ERR_CUDA;
-    return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(kUThreads), L::SMEM_BYTES, st, pl.ranks,
+    // A grid that needs fewer CTAs per SM than would fit is spread evenly by asking for more
+    // shared memory than the kernel uses: 256 CTAs land two per SM on 108 SMs and one on 40
+    // instead of three on some and none on others (clusters are otherwise packed densely).
+    size_t smem = L::SMEM_BYTES;
+    const int ctas = pl.n_tiles * pl.ranks * pl.m_tiles;
+    const int per_sm = cdiv(ctas, kNumSMs);
+#ifdef LQ2_TUNING
+    if (!getenv("LQ2_U_NOSPREAD"))
+#endif
+    if (per_sm < resident_ctas(MB)) smem = std::max(smem, size_t(kMaxSmemPerCta / per_sm - 1024));
+    return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(kUThreads), smem, st, pl.ranks,
                       map_w, map_x, map_s, map_z, p);
 }
 

@@ -439,16 +439,20 @@ def run_case(args):
         with torch.cuda.graph(graph, stream=side):
             for c in calls:
                 c()
-        graph.replay()
+        for _ in range(3):
+            graph.replay()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(side)
-        graph.replay()
-        b.record(side)
-        torch.cuda.synchronize()
-    us = a.elapsed_time(b) * 1e3 / len(calls)
+        times = []
+        for _ in range(5):
+            a.record(side)
+            graph.replay()
+            b.record(side)
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+    us = sorted(times)[len(times) // 2] * 1e3 / len(calls)
     gbs = nbytes / us / 1e3
-    print(json.dumps({"case": args.case, "workload": what, "launches_timed": len(calls),
+    print(json.dumps({"case": args.case, "workload": what, "launches_timed": len(calls), "replays": "median of 5",
                       "us_per_launch": round(us, 2), "algorithmic_bytes_per_launch": nbytes,
                       "achieved_gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 4), "of": which}),
           flush=True)

@@ -133,9 +133,10 @@ struct Layout {
 #else
     static constexpr int STAGES = NJ <= 2 ? 4 : 3;
 #endif
-    static constexpr int RED_BYTES = MT * TN * 4;
+    static constexpr int RED_BYTES = MT * TN * 4;               // receive area of the split-K reduction
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-    static constexpr int DATA_BYTES = RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES;
+    static constexpr int RECV_OFF = RING_BYTES;                 // never aliased with the ring: peers write into it
+    static constexpr int DATA_BYTES = RING_BYTES + RED_BYTES;
     static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + 2 * STAGES * 8;   // alignment slack + mbarriers
 };
 
@@ -181,6 +182,9 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     __syncthreads();
+    // first half of a cluster barrier: by the time the epilogue waits for it, every CTA of
+    // the cluster is known to be running, which remote shared-memory stores require
+    if (ranks > 1) asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
 
     float acc[2][NJW][4];
 #pragma unroll
@@ -361,36 +365,41 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
         return;
     }
 
-    // ---- cluster reduction through distributed shared memory
+    // ---- split-K reduction.  Rank q of the cluster owns columns [q * W, (q + 1) * W) of the tile.
+    // Every rank writes its partial sums for those columns straight from registers into q's
+    // receive area (remote shared memory), one cluster barrier follows, and q adds the ranks'
+    // parts in rank order.  Nobody reads remote memory after the barrier, so a CTA may leave as
+    // soon as it has written its slice.
     cg::cluster_group cluster = cg::this_cluster();
-    __syncthreads();                                   // every warp is done with the ring
-    float* red = reinterpret_cast<float*>(smem);       // [MT][TN]
+    const int W = TN / ranks;
+    float* recv = reinterpret_cast<float*>(smem + L::RECV_OFF);       // [ranks][MT][W]
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");   // all CTAs of the cluster are running
     if (warp < CONSUMERS) {
+        const int col = slab * 32 + 4 * g;
+        const int dest = col / W, c = col - dest * W;
+        float* dst = cluster.map_shared_rank(recv, dest) + size_t(rank) * MT * W + c;
 #pragma unroll
         for (int j = 0; j < NJW; ++j) {
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 const int ml = 8 * (jpart * NJW + j) + 2 * t + r;
-                *reinterpret_cast<float4*>(red + ml * TN + slab * 32 + 4 * g) =
+                *reinterpret_cast<float4*>(dst + ml * W) =
                     make_float4(acc[0][j][r], acc[0][j][2 + r], acc[1][j][r], acc[1][j][2 + r]);
             }
         }
     }
-    cluster.sync();
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
     {
-        // rank r finishes column quads [q0, q1) of the tile
-        constexpr int QUADS = TN / 4;
-        const int q0 = rank * QUADS / ranks, q1 = (rank + 1) * QUADS / ranks;
-        const int quads = q1 - q0;
+        const int quads = W / 4;
         for (int e = tid; e < rows * quads; e += L::THREADS) {
-            const int ml = e / quads, col = (q0 + e % quads) * 4;
+            const int ml = e / quads, col = (e - ml * quads) * 4;
             float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int q = 0; q < ranks; ++q) {
-                const float* remote = cluster.map_shared_rank(red, q);
-                const float4 v = *reinterpret_cast<const float4*>(remote + ml * TN + col);
+                const float4 v = *reinterpret_cast<const float4*>(recv + (size_t(q) * MT + ml) * W + col);
                 sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
             }
-            const int nn = tile_n0 + col;
+            const int nn = tile_n0 + rank * W + col;
             if (nn < p.n) {
                 const __half2 lo = __floats2half2_rn(sum.x, sum.y);
                 const __half2 hi = __floats2half2_rn(sum.z, sum.w);
@@ -398,7 +407,6 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
             }
         }
     }
-    cluster.sync();                                    // nobody leaves while its tile is still being read
 }
 
 struct Plan {
@@ -472,7 +480,7 @@ int launch_one(const W4Params& p, const Plan& pl, cudaStream_t st) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LQ2_ERR_CUDA;
     if (!configured[dev]) {
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES) != cudaSuccess)
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
             return LQ2_ERR_CUDA;
         // several CTAs per SM are planned for: ask for the largest shared-memory carve-out
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -489,7 +497,16 @@ int launch_one(const W4Params& p, const Plan& pl, cudaStream_t st) {
     ok = ok && make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ZTABLE ? p.zeros : p.scales, n, groups, n * 2,
                         L::TN, GPS, false);
     if (!ok) return LQ2_ERR_CUDA;
-    return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(L::THREADS), L::SMEM_BYTES, st, pl.ranks,
+    // A grid that needs fewer CTAs per SM than would fit is spread evenly over the SMs by
+    // asking for more shared memory than the kernel uses (clusters are otherwise packed densely).
+    size_t smem = L::SMEM_BYTES;
+    const int per_sm = cdiv(pl.n_tiles * pl.ranks * pl.m_tiles, kNumSMs);
+    constexpr int kResident = NJ <= 2 ? 4 : (NJ == 4 ? 3 : 1);
+#ifdef LQ2_TUNING
+    if (!getenv("LQ2_W4_NOSPREAD"))
+#endif
+    if (per_sm < kResident && size_t(227 * 1024 / per_sm - 1024) > smem) smem = size_t(227 * 1024 / per_sm - 1024);
+    return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(L::THREADS), smem, st, pl.ranks,
                       map_w, map_x, map_s, map_z, p);
 }
 

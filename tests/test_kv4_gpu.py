@@ -147,6 +147,9 @@ def build_case(bs, lens, m, hq, hkv, d, page, group, seed, width=None):
     (2, [1, 500], 1, 4, 4, 64, 32, 32),         # no GQA, single-token context, D = 64
     (4, [0, 5, 0, 40], 1, 8, 2, 128, 16, 128),  # empty sequences yield zeros
     (2, [120, 64], 3, 8, 2, 128, 64, 64),       # odd verify width
+    (4, [2100, 700, 2049, 33], 1, 4, 1, 128, 256, 64),   # one KV head per rank: Qwen3-8B at TP = 8
+    (2, [2100, 300], 16, 4, 1, 128, 256, 64),   # the same, 16-position verify
+    (3, [1500, 2100, 9], 1, 8, 2, 128, 256, 64),         # TP = 4
 ])
 def test_attention_against_oracle(bs, lens, m, hq, hkv, d, page, group):
     from linkq2_b200.kernels.kv4 import paged_attention_decode

@@ -87,6 +87,24 @@ def test_projection_shapes_decode_and_batch(k, n, affine):
         assert ow.rel_l2(y, expected) < TOL
 
 
+@pytest.mark.parametrize("k,n", [(4096, 768), (512, 4096), (4096, 3072), (1536, 4096),      # Qwen3-8B at TP = 8
+                                 (4096, 1536), (1024, 4096), (4096, 6144), (3072, 4096),     # TP = 4
+                                 (2048, 4096), (4096, 12288), (6144, 4096)])                 # TP = 2
+def test_tensor_parallel_shard_shapes(k, n):
+    """Per-rank projection shapes of Qwen3-8B under tensor parallelism 2, 4 and 8 (fused
+    qkv / gate_up columns, row-split o / down) at M = 1, 32 and 512."""
+    w = ow.seeded_weight(n, k, seed=k + n)
+    values, scale = ow.rtn_quantize(w, 128)
+    layer = make_layer(values, scale, None, 128, True)
+    dense = ow.dequantize_fp32(values, scale, symmetric=True)
+    for m in (1, 32, 512):
+        x = ow.seeded_activation(m, k, seed=m, outliers=True)
+        y = layer(x.cuda()).float().cpu()
+        expected = ow.linear_fp32(x, dense)
+        assert ow.error_over_rms(y, expected) <= TOL
+        assert ow.rel_l2(y, expected) < TOL
+
+
 def test_linearity_and_determinism():
     """Size-independent properties: the op is linear in x up to fp16 rounding
     of the output, and repeated calls return identical bits (split-K partials

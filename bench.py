@@ -293,7 +293,7 @@ def run_b200(args):
             s.append(tok)
 
     # ---- e2e: K more steps through the public host API
-    h2d = BATCH * (8 + 8 + 4 + 4) + BATCH * len(seqs[0].block_table) * 4
+    h2d = BATCH * 4 * 4 + BATCH * len(seqs[0].block_table) * 4          # one packed int32 record per step
     d2h = BATCH * 8
     barrier()
     ev0.record()

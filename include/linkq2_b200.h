@@ -248,6 +248,19 @@ int lq2_pre_attention(const void* q, const void* k, const void* v, int64_t q_str
                       uint32_t* vq, void* vs, const int32_t* slots, int tokens, int hq, int hkv, int d,
                       int v_group, int64_t num_slots, float eps, void* stream);
 
+/*
+ * Fills the fixed input buffers of a captured decode graph for one step, replacing the
+ * seven device copies of CUDAGraphs.replay (qslab/runtime/execute/cuda_graph.py:60-72).
+ * packed (device, int32): [batch ids | batch positions | batch slots | batch context
+ * lengths | batch x width block-table entries].  Rows batch..rows_cap-1 get slot -1 and
+ * context length 0, table entries outside [batch, width] get 0, as the reference pads.
+ * input_ids, positions [rows_cap] int64; slot_mapping, context_lens [rows_cap] int32;
+ * block_tables [rows_cap, width_cap] int32.
+ */
+int lq2_stage_decode(const int32_t* packed, int64_t* input_ids, int64_t* positions, int32_t* slot_mapping,
+                     int32_t* context_lens, int32_t* block_tables, int batch, int rows_cap, int width,
+                     int width_cap, void* stream);
+
 /* --------------------------------------------------------------------------
  * Tensor-parallel exchange.  No counterpart in the reference, which is
  * single-GPU (qslab/runtime/model/qwen3.py:1-5): the sum all-reduce of the

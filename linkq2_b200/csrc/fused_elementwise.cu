@@ -10,6 +10,8 @@
 // Each kernel below keeps the reference's rounding points: statistics and
 // rotations in fp32, a cast to fp16 after the normalisation, fp16 products with
 // the norm weight and with lambda, fp16 result of SiLU before the product.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace lq2 {
@@ -266,6 +268,34 @@ __global__ void __launch_bounds__(128) pre_attention_kernel(const PreAttnParams 
     }
 }
 
+// ---------------------------------------------------------------- decode step staging
+// One launch fills the fixed input buffers of a captured decode graph from one packed
+// int32 record [ids | positions | slots | context lens | block tables (batch x width)],
+// including the padding of the unused rows (slot -1, context length 0, table 0), which
+// the reference does with seven small device copies (cuda_graph.py:60-72).
+__global__ void __launch_bounds__(256) stage_decode_kernel(const int32_t* __restrict__ packed, int64_t* input_ids,
+                                                           int64_t* positions, int32_t* slot_mapping,
+                                                           int32_t* context_lens, int32_t* block_tables,
+                                                           int batch, int rows_cap, int width, int width_cap) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int total = rows_cap * width_cap;
+    if (i < rows_cap) {
+        const bool live = i < batch;
+        if (live) {
+            input_ids[i] = packed[i];
+            positions[i] = packed[batch + i];
+        }
+        slot_mapping[i] = live ? packed[2 * batch + i] : -1;
+        context_lens[i] = live ? packed[3 * batch + i] : 0;
+    }
+    if (i < total) {
+        const int r = i / width_cap, c = i - r * width_cap;
+        block_tables[i] = (r < batch && c < width) ? packed[4 * batch + r * width + c] : 0;
+    }
+}
+
 }  // namespace
 }  // namespace lq2
 
@@ -329,6 +359,18 @@ int lq2_pre_attention(const void* q, const void* k, const void* v, int64_t q_str
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (d == 128) return launch_pdl(pre_attention_kernel<128>, dim3(blocks), dim3(128), 0, st, 1, p);
     return launch_pdl(pre_attention_kernel<64>, dim3(blocks), dim3(128), 0, st, 1, p);
+}
+
+int lq2_stage_decode(const int32_t* packed, int64_t* input_ids, int64_t* positions, int32_t* slot_mapping,
+                     int32_t* context_lens, int32_t* block_tables, int batch, int rows_cap, int width,
+                     int width_cap, void* stream) {
+    if (!packed || !input_ids || !positions || !slot_mapping || !context_lens || !block_tables) return LQ2_ERR_ARG;
+    if (batch < 0 || rows_cap <= 0 || batch > rows_cap || width < 0 || width_cap <= 0 || width > width_cap)
+        return LQ2_ERR_SHAPE;
+    const int64_t total = std::max<int64_t>(rows_cap, int64_t(rows_cap) * width_cap);
+    return launch_pdl(stage_decode_kernel, dim3(unsigned(cdiv64(total, 256))), dim3(256), 0,
+                      static_cast<cudaStream_t>(stream), 1, packed, input_ids, positions, slot_mapping, context_lens,
+                      block_tables, batch, rows_cap, width, width_cap);
 }
 
 }  // extern "C"

@@ -12,7 +12,7 @@
 //
 // Orientation.  The product is computed transposed, Y^T[n, m] = W[n, :] . X[m, :],
 // so that the 128 rows of the MMA are output channels and its N dimension
-// (16..256) is the batch: a 32-row decode batch wastes nothing.  Per CTA: 128
+// (16..128) is the batch: a 32-row decode batch wastes nothing.  Per CTA: 128
 // output channels x MB batch rows, K streamed in stages of 64.
 //
 // Warp roles (10 warps):
@@ -225,7 +225,7 @@ __device__ __forceinline__ void stamp(int slot) {
 
 // CTAs per SM the plan counts on (shared memory and tensor-memory columns allow them; the
 // launch bounds make the register allocation follow)
-__host__ __device__ constexpr int resident_ctas(int mb) { return mb <= 32 ? 3 : (mb <= 64 ? 2 : 1); }
+__host__ __device__ constexpr int resident_ctas(int mb) { return mb <= 32 ? 3 : (mb <= 128 ? 2 : 1); }
 
 template <int MB, bool ZTABLE, int GPSU>
 __global__ void __launch_bounds__(kUThreads, resident_ctas(MB))
@@ -578,7 +578,12 @@ struct UPlan {
 // keeps the grid within one resident wave and leaves every rank at least four stages.
 UPlan make_uplan(int m, int n, int k) {
     UPlan p;
-    p.mb = m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : (m <= 128 ? 128 : 256)));
+    // 128-row batch tiles at two CTAs per SM beat 256-row tiles at one at every M measured
+    // (gate_up geometry: 126 vs 159 us at M = 512, 439 vs 522 us at M = 2048)
+    p.mb = m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : 128));
+#ifdef LQ2_TUNING
+    if (const char* e = getenv("LQ2_U_MB")) p.mb = atoi(e);
+#endif
     p.m_tiles = cdiv(m, p.mb);
     p.n_tiles = cdiv(n, kUM);
     const int stages = cdiv(k, stage_k(p.mb));
@@ -662,8 +667,7 @@ int w4a16_umma_launch(const __half* x, int64_t ldx, const int32_t* packed, const
         case 16: return launch_umma_z<16>(x, ldx, packed, scales, zeros, p, pl, st);
         case 32: return launch_umma_z<32>(x, ldx, packed, scales, zeros, p, pl, st);
         case 64: return launch_umma_z<64>(x, ldx, packed, scales, zeros, p, pl, st);
-        case 128: return launch_umma_z<128>(x, ldx, packed, scales, zeros, p, pl, st);
-        default: return launch_umma_z<256>(x, ldx, packed, scales, zeros, p, pl, st);
+        default: return launch_umma_z<128>(x, ldx, packed, scales, zeros, p, pl, st);
     }
 }
 

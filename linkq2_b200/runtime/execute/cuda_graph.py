@@ -109,6 +109,20 @@ class CUDAGraphs:
         b['block_tables'][:batch, :block_tables.size(1)] = block_tables
         return next(bs for bs in self.batch_sizes if bs >= batch)
 
+    def stage_packed(self, packed: torch.Tensor, batch: int, width: int):
+        """The same as ``stage`` for a decode step whose metadata arrive as one packed
+        int32 device record ``[ids | positions | slots | context lens | block tables]``:
+        one kernel fills the fixed buffers, padding included (``lq2_stage_decode``)."""
+        b = self.families[1].buffers
+        with torch.cuda.device(self.device):
+            status = _lib.lib.lq2_stage_decode(
+                packed.data_ptr(), b['input_ids'].data_ptr(), b['positions'].data_ptr(),
+                b['slot_mapping'].data_ptr(), b['context_lens'].data_ptr(), b['block_tables'].data_ptr(),
+                batch, self.max_batch, width, self.blocks, torch.cuda.current_stream().cuda_stream)
+        _lib.check(status, "lq2_stage_decode")
+        _lib.count()
+        return next(bs for bs in self.batch_sizes if bs >= batch)
+
     def run_graph(self, rows, bucket):
         self.families[rows].graphs[bucket].replay()
         _lib.count(self.kernels_per_graph[(rows, bucket)])

@@ -43,6 +43,7 @@ class ModelRunner:
         self.tp = get_tp()
         self.graph_replays = 0
         self.last_logits = None
+        self._pinned = self._pinned_np = self._packed_dev = None
         self.allocate_kv_cache()
         self.load_smoothing(smooth_kv)
         # The checkpoint is loaded and nothing writes the quantized weights from here on:
@@ -185,12 +186,46 @@ class ModelRunner:
     def run(self, seqs: list[Sequence], is_prefill: bool, counts: list[int] | None = None) -> list[int]:
         """One step; returns one greedy token per sequence (for prefill: the token
         after the last scheduled position)."""
+        graphs = self.cuda_graphs
+        if not is_prefill and graphs is not None and len(seqs) <= max(graphs.batch_sizes):
+            return self._finish(seqs, self._decode_packed(seqs), False, None)
         if is_prefill:
             counts = counts or [len(s) - s.num_cached_tokens for s in seqs]
             input_ids, positions = self.prepare_prefill(seqs, counts)
         else:
             input_ids, positions = self.prepare_decode(seqs)
         hidden = self.run_model(input_ids, positions, is_prefill)
+        return self._finish(seqs, hidden, is_prefill, counts)
+
+    def _decode_packed(self, seqs: list[Sequence]):
+        """Decode step through the graphs with one pinned record, one host-to-device copy
+        and one staging kernel instead of five copies and seven staging ops."""
+        graphs = self.cuda_graphs
+        b = len(seqs)
+        width = max(len(seq.block_table) for seq in seqs)
+        if self._pinned is None:
+            cap = graphs.max_batch * (4 + graphs.blocks)
+            self._pinned = torch.empty(cap, dtype=torch.int32, pin_memory=True)
+            self._pinned_np = self._pinned.numpy()
+            self._packed_dev = torch.empty(cap, dtype=torch.int32, device=self.device)
+        rec = self._pinned_np
+        rec[0:b] = [seq.last_token for seq in seqs]
+        rec[b:2 * b] = [len(seq) - 1 for seq in seqs]
+        rec[2 * b:3 * b] = [seq.slot(len(seq) - 1) for seq in seqs]
+        rec[3 * b:4 * b] = [len(seq) for seq in seqs]
+        tables = rec[4 * b:4 * b + b * width].reshape(b, width)
+        for i, seq in enumerate(seqs):
+            n = len(seq.block_table)
+            tables[i, :n] = seq.block_table
+            tables[i, n:] = -1
+        n = 4 * b + b * width
+        self._packed_dev[:n].copy_(self._pinned[:n], non_blocking=True)
+        bucket = graphs.stage_packed(self._packed_dev, b, width)
+        graphs.run_graph(1, bucket)
+        self.graph_replays += 1
+        return graphs.families[1].buffers['outputs'][:b]
+
+    def _finish(self, seqs, hidden, is_prefill, counts):
         if is_prefill:
             hidden = hidden[(get_context().cu_seqlens_q[1:] - 1).long()]
             for seq, n in zip(seqs, counts):

@@ -24,6 +24,9 @@
 // partial (O, max, denominator) per row, takes a ticket, and the last CTA of a
 // (sequence, KV head) merges the partials in split order and writes fp16.
 #include <math.h>
+#ifdef LQ2_TUNING
+#include <stdlib.h>
+#endif
 
 #include <mutex>
 
@@ -779,13 +782,18 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
     if (tid == 0) *counter = 0;
 }
 
-// KV heads per CTA for the fast path: as many as possible (their rows are adjacent in
-// memory) while the grid can still fill the machine twice.
+// KV heads per CTA for the fast path.  Measured at Qwen3-8B geometry: the best grids have
+// about one resident wave of CTAs (two per SM) with as few splits as possible - batch 32 x
+// 2.1 k tokens: 29 us with one head per CTA and no split against 32 us with two heads and two
+// splits; batch 64 x 4 k: 85 us with two heads per CTA and no split against 100 us with eight
+// heads and four splits.  So: the fewest heads per CTA whose grid still fits one wave.
 int fast_heads_per_cta(int batch, int hkv, int64_t capacity) {
+    (void)capacity;
+#ifdef LQ2_TUNING
+    if (const char* e = getenv("LQ2_ATTN_HPC")) return atoi(e);
+#endif
     int hpc = 1;
-    while (hpc * 2 <= 8 && hkv % (hpc * 2) == 0) hpc *= 2;
-    const int64_t max_splits = capacity / 512 > 0 ? (capacity / 512 < 64 ? capacity / 512 : 64) : 1;
-    while (hpc > 1 && int64_t(batch) * (hkv / hpc) * max_splits < 2 * kNumSMs) hpc /= 2;
+    while (hpc < 8 && hkv % (hpc * 2) == 0 && int64_t(batch) * (hkv / hpc) > 2 * kNumSMs) hpc *= 2;
     return hpc;
 }
 
@@ -803,21 +811,31 @@ int row_tiles(int m, int hq, int hkv) {
 }  // namespace
 
 int kv4_attention_splits(int batch, int m, int hq, int hkv, int d, int page, int max_blocks) {
-    (void)d; (void)m; (void)hq;
+    (void)d;
     const int64_t capacity = int64_t(max_blocks) * page;
-    // Shapes only.  A CTA covers hpc KV heads with 8 / hpc warps per head; enough splits
-    // to fill the machine twice, no warp longer than 1024 tokens (so one long sequence in
-    // a batch cannot become the tail), never less than 256 tokens of capacity per split.
-    const int hpc = fast_heads_per_cta(batch, hkv, capacity);
-    const int wt = 8 / hpc;
+    // Shapes only.  Enough splits to fill one resident wave (two CTAs per SM), no warp longer
+    // than 1024 tokens (so one long sequence in a batch cannot become the tail), never less
+    // than 256 tokens of capacity per split.
+    const bool fast = m * (hq / hkv) <= 8 && page % kFastTile == 0;
+    int hpc, wt;
+    if (fast) {
+        hpc = fast_heads_per_cta(batch, hkv, capacity);
+        wt = 8 / hpc;
+    } else {                                             // 4-warp CTAs, one KV head each
+        hpc = 1;
+        wt = 2;
+    }
     const int base = batch * (hkv / hpc);
-    int64_t splits = 2 * kNumSMs / base;                 // floor: the grid stays within one resident wave
+    int64_t splits = (fast ? 2 : 4) * kNumSMs / base;    // floor: the grid stays within one resident wave
     const int64_t by_len = cdiv64(capacity, int64_t(1024) * wt);
     if (by_len > splits) splits = by_len;
     const int64_t most = capacity / 256 > 0 ? capacity / 256 : 1;
     if (splits > most) splits = most;
     if (splits > 64) splits = 64;
     if (splits < 1) splits = 1;
+#ifdef LQ2_TUNING
+    if (const char* e = getenv("LQ2_ATTN_SPLITS")) splits = atoi(e);
+#endif
     return int(splits);
 }
 

@@ -568,24 +568,25 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
         cp_async_commit();
     }
 
-    for (int it = 0; it < n_my; ++it) {
-        const int slot = it % kFastStages;
+    // The loop is unrolled over the ring so that the stage slot, its shared-memory address and
+    // its entry of the register ring of scales are compile-time constants.
+    for (int it0 = 0; it0 < n_my; it0 += kFastStages) {
+#pragma unroll
+      for (int slot = 0; slot < kFastStages; ++slot) {
+        const int it = it0 + slot;
+        if (it >= n_my) break;
         {
             const int nxt = it + kFastStages - 1;
-            // the register ring of scales rotates with the stages: entry (nxt % stages)
+            constexpr int kPrev = kFastStages - 1;
+            const int nslot = (slot + kPrev) % kFastStages;
             uint32_t sc_new = 0;
-            if (nxt < n_my) issue(nxt, nxt % kFastStages, sc_new);
+            if (nxt < n_my) issue(nxt, nslot, sc_new);
             cp_async_commit();
-#pragma unroll
-            for (int i = 0; i < kFastStages; ++i)
-                if (i == nxt % kFastStages) sc_ring[i] = sc_new;
+            sc_ring[nslot] = sc_new;
         }
         cp_async_wait<kFastStages - 1>();
         __syncwarp();
-        uint32_t sc_cur = 0;
-#pragma unroll
-        for (int i = 0; i < kFastStages; ++i)
-            if (i == slot) sc_cur = sc_ring[i];
+        const uint32_t sc_cur = sc_ring[slot];
         if ((live_bits >> slot) & 1u) {
             const unsigned char* kb = ring + slot * L::STAGE_BYTES;
             const unsigned char* vb = kb + L::K_BYTES;
@@ -682,6 +683,7 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
             }
         }
         __syncwarp();
+      }
     }
     cp_async_wait<0>();
 

@@ -116,7 +116,6 @@ template <int NJ, int WN, int GPS>
 struct Layout {
     static constexpr int MT = 8 * NJ;
     static constexpr int TN = 32 * WN;
-    static constexpr int KS = 1;                                // (one consumer warp per k range of a stage)
     static constexpr int NJW = NJ < 2 ? NJ : 2;                 // 8-row activation blocks per consumer warp
     static constexpr int JS = NJ / NJW;                         // consumer warps that share a slab, splitting the rows
     static constexpr int CONSUMERS = WN * JS;
@@ -149,9 +148,9 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
                     const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                     const W4Params p) {
     using L = Layout<NJ, WN, GPS>;
-    constexpr int MT = L::MT, TN = L::TN, STAGES = L::STAGES, KS = L::KS, CONSUMERS = L::CONSUMERS, NJW = L::NJW;
+    constexpr int MT = L::MT, TN = L::TN, STAGES = L::STAGES, CONSUMERS = L::CONSUMERS, NJW = L::NJW;
     constexpr int STEPS_PER_GROUP = 4 / GPS;
-    constexpr int STEPS = 4 / KS;                            // 32-k steps of a stage done by one consumer warp
+    constexpr int STEPS = 4;                                 // 32-k steps of a stage
     // k8 row (and activation chunk) that lane t uses in step kk.  Rows 2t + (kk & 1) of an
     // 8-row block make the swizzled 128-bit reads conflict-free; with four groups per
     // stage a step must stay inside 4 consecutive rows instead.
@@ -195,7 +194,6 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
             for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
 
     const int slab = warp % WN, jpart = warp / WN;           // first activation block of this warp: jpart * NJW
-    constexpr int kpart = 0;
     if (warp == CONSUMERS) {
         // ------------------------------------------------------------ producer
         // Out-of-range rows and columns are zero-filled by the TMA unit and still count
@@ -266,8 +264,7 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
             if (p.m < 0)
 #endif
 #pragma unroll
-            for (int ks = 0; ks < STEPS; ++ks) {
-                const int kk = kpart * STEPS + ks;
+            for (int kk = 0; kk < STEPS; ++kk) {
                 const int row = INTERLEAVE ? 8 * (kk >> 1) + 2 * t + (kk & 1) : 4 * kk + t;
                 // 128B swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
                 const uint4 wq = *reinterpret_cast<const uint4*>(wsm + row * 128 + ((g ^ (row & 7)) << 4));
@@ -309,7 +306,7 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
 #endif
                 // end of a scale group, or of this warp's share of one (the scale then multiplies a
                 // partial sum, which is the same by linearity)
-                if ((ks + 1) % (STEPS_PER_GROUP < STEPS ? STEPS_PER_GROUP : STEPS) == 0) {
+                if ((kk + 1) % (STEPS_PER_GROUP < STEPS ? STEPS_PER_GROUP : STEPS) == 0) {
                     const int gq = kk / STEPS_PER_GROUP;
                     const uint2 sc = *reinterpret_cast<const uint2*>(ssm + gq * TN * 2);
                     uint2 zc = make_uint2(0x48004800u, 0x48004800u);           // 8.0 x4
@@ -346,7 +343,7 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
     const int n0 = nb + 4 * g;
 
     // ---- write-out.  Consumer lane (g, t) owns columns n0..n0+3 of rows m0 + 8j + 2t (+1).
-    if (ranks == 1 && KS == 1) {
+    if (ranks == 1) {
         if (n_ok) {
 #pragma unroll
             for (int j = 0; j < NJW; ++j) {

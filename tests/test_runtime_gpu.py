@@ -156,3 +156,36 @@ def test_smoothing_validation_and_lambda(tmp_path):
         ModelRunner(model, rc, smooth_kv={"lambda": torch.ones(2, 1, 64), "kscale": torch.zeros(2, 1, 64)})
     with pytest.raises(ValueError):
         ModelRunner(model, RunnerConfig(kvcache_block_size=96, num_kvcache_blocks=8), smooth_kv=None)
+
+
+def test_packed_decode_staging_equals_the_seven_copies(tmp_path):
+    """``lq2_stage_decode`` (one packed record, one kernel) leaves the graph's fixed
+    buffers exactly as ``CUDAGraphs.stage`` (the reference's seven device copies,
+    cuda_graph.py:60-72) does, padding rows included."""
+    write_checkpoint(tmp_path / "w4")
+    runner = make_runner(tmp_path / "w4", eager=False)
+    graphs = runner.cuda_graphs
+    buffers = graphs.families[1].buffers
+    g = torch.Generator().manual_seed(9)
+    for batch, width in [(1, 1), (3, 2), (4, 4), (2, 3)]:
+        ids = torch.randint(0, 127, (batch,), generator=g)
+        pos = torch.randint(0, 500, (batch,), generator=g)
+        slots = torch.randint(-1, 2000, (batch,), generator=g, dtype=torch.int32)
+        lens = torch.randint(0, 500, (batch,), generator=g, dtype=torch.int32)
+        tables = torch.randint(-1, 16, (batch, width), generator=g, dtype=torch.int32)
+        for name in buffers:                                   # stale content from another step
+            if name != "outputs":
+                buffers[name].fill_(77)
+        graphs.stage(ids.cuda(), pos.cuda(), slots.cuda(), lens.cuda(), tables.cuda(), 1)
+        torch.cuda.synchronize()
+        expected = {k: v.clone() for k, v in buffers.items() if k != "outputs"}
+        for name in expected:
+            buffers[name].fill_(55)
+        packed = torch.cat([ids.int(), pos.int(), slots, lens, tables.flatten()]).cuda()
+        graphs.stage_packed(packed, batch, width)
+        torch.cuda.synchronize()
+        for name, want in expected.items():
+            got = buffers[name]
+            if name in ("input_ids", "positions"):             # rows beyond the batch are never read
+                got, want = got[:batch], want[:batch]
+            assert torch.equal(got, want), name

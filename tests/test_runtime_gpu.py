@@ -158,6 +158,7 @@ def test_smoothing_validation_and_lambda(tmp_path):
         ModelRunner(model, RunnerConfig(kvcache_block_size=96, num_kvcache_blocks=8), smooth_kv=None)
 
 
+@torch.inference_mode()
 def test_packed_decode_staging_equals_the_seven_copies(tmp_path):
     """``lq2_stage_decode`` (one packed record, one kernel) leaves the graph's fixed
     buffers exactly as ``CUDAGraphs.stage`` (the reference's seven device copies,

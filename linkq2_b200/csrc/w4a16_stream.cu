@@ -253,9 +253,13 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
         const __half2 k16th = __floats2half2_rn(0.0625f, 0.0625f);
         constexpr uint32_t kOnes = 0x3C003C00u;
         constexpr float kTwo24 = 16777216.f;
-        for (int it = 0; it < my_stages; ++it) {
-            const int slot = it % STAGES;
-            mbar_wait(bars + 8 * slot, (it / STAGES) & 1);
+        // unrolled over the ring: the stage slot and its addresses are compile-time constants
+        uint32_t ring_phase = 0;                              // (it / STAGES) & 1
+        for (int it0 = 0; it0 < my_stages; it0 += STAGES, ring_phase ^= 1u) {
+#pragma unroll
+          for (int slot = 0; slot < STAGES; ++slot) {
+            if (it0 + slot >= my_stages) break;
+            mbar_wait(bars + 8 * slot, ring_phase);
             const unsigned char* base = smem + slot * L::STAGE_BYTES;
             const unsigned char* wsm = base + slab * L::SLAB_BYTES;
             const unsigned char* xsm = base + L::W_BYTES;
@@ -335,6 +339,7 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(bars + 8 * (STAGES + slot));
+          }
         }
     }
 

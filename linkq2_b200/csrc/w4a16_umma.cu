@@ -327,8 +327,13 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
         // ------------------------------------------------------------ MMA issuer
         pdl_wait();
         constexpr uint32_t idesc = umma_idesc(kUM, MB);
-        for (int it = 0; it < my_stages; ++it) {
-            const int rslot = it % RS, aslot = it % AS;
+        constexpr int U = AS == 1 ? RS : 1;                   // unrolled over the raw ring, as the dequantisers are
+        for (int it0 = 0; it0 < my_stages; it0 += U) {
+#pragma unroll
+          for (int us = 0; us < U; ++us) {
+            const int it = it0 + us;
+            if (it >= my_stages) break;
+            const int rslot = U == 1 ? it % RS : us, aslot = it % AS;
             mbar_wait_bounded(a_full(aslot), (it / AS) & 1);
             tc_fence_after();
             if (lane == 0) {
@@ -349,6 +354,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                 if (it == my_stages - 1) umma_commit(acc_full);
             }
             __syncwarp();
+          }
         }
     } else {
         // ------------------------------------------------------------ dequantise
@@ -369,10 +375,18 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             __syncwarp();
             if (lane == 0) mbar_arrive(a_full(it_done % AS));
         };
-        for (int it = 0; it < my_stages; ++it) {
-            const int rslot = it % RS, aslot = it % AS;
+        // With a single A tile the loop is unrolled over the raw ring, which makes the stage
+        // slot, its shared-memory addresses and its barrier compile-time constants.
+        constexpr int U = AS == 1 ? RS : 1;
+        uint32_t ring_phase = 0;                              // (it / RS) & 1 when U == RS
+        for (int it0 = 0; it0 < my_stages; it0 += U, ring_phase ^= 1u) {
+#pragma unroll
+          for (int us = 0; us < U; ++us) {
+            const int it = it0 + us;
+            if (it >= my_stages) break;
+            const int rslot = U == 1 ? it % RS : us, aslot = it % AS;
             const unsigned char* rbase = r_ring + rslot * L::R_STAGE_BYTES;
-            mbar_wait_bounded(raw_full(rslot), (it / RS) & 1);
+            mbar_wait_bounded(raw_full(rslot), U == 1 ? uint32_t(it / RS) & 1u : ring_phase);
             LQ2_STAMP(3, it == 0 && warp == 2 && lane == 0);           // first stage landed
             const uint32_t* raw = reinterpret_cast<const uint32_t*>(rbase + L::RAW_OFF);
             const __half* sc = reinterpret_cast<const __half*>(rbase + L::S_OFF);
@@ -426,6 +440,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                 tmem_st16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + aslot * L::A_COLS +
                               khalf * (UK / 4) + 16 * b, cols);
             }
+          }
         }
         if (my_stages > 0) publish(my_stages - 1);
     }

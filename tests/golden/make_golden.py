@@ -20,7 +20,9 @@ os.environ["TRITON_INTERPRET"] = "1"
 import numpy as np
 import torch
 
-REFERENCE = os.environ.get("LINKQ2_REFERENCE", "/root/reference")
+REFERENCE = os.environ.get("LINKQ2_REFERENCE")          # a checkout of chuoer47/LinkQ2
+if not REFERENCE:
+    raise SystemExit("set LINKQ2_REFERENCE to a checkout of the reference (the directory that holds qslab/)")
 sys.path.insert(0, REFERENCE)
 OUT = Path(__file__).resolve().parent
 

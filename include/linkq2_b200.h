@@ -99,6 +99,20 @@ int lq2_w4a16_linear(const void* x, int64_t x_row_stride, const int32_t* packed,
                      const void* scales, const void* zeros, void* y, int m, int n, int k,
                      int group, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * The gate and up projections of Qwen3MLP and the activation between them in one launch,
+ * replacing F.silu(gate_proj(x)) * up_proj(x) (qslab/runtime/model/qwen3.py:59-64):
+ *   y[M, N/2][m, 4b + j] = fp16(silu(fp32(g))) * u,  g = z[m, 8b + j], u = z[m, 8b + 4 + j],
+ *   z = fp16(x . dequant(W)^T) as lq2_w4a16_linear would have written it.
+ * packed / scales / zeros are the two projections' buffers with their columns interleaved in
+ * blocks of four, [g0..g3 | u0..u3 | g4..g7 | u4..u7 | ...] (a load-time layout step on the
+ * [K/8, N] buffers, nothing is repacked); N = 2 * intermediate size, a multiple of 64.
+ * Other arguments as lq2_w4a16_linear.
+ */
+int lq2_w4a16_gate_up_silu(const void* x, int64_t x_row_stride, const int32_t* packed,
+                           const void* scales, const void* zeros, void* y, int m, int n, int k,
+                           int group, void* workspace, size_t workspace_bytes, void* stream);
+
 /* --------------------------------------------------------------------------
  * KV4 cache.  Pool layout (qslab/runtime/execute/model_runner.py:146-156):
  *   kq, vq  [S, HKV, D/8] 32-bit words, 8 offset-binary nibbles per word

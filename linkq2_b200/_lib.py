@@ -32,6 +32,8 @@ SIGNATURES = {
     "lq2_w4a16_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "lq2_w4a16_linear": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "lq2_w4a16_gate_up_silu": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "lq2_kv4_store": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p]),
     "lq2_kv4_attention_splits": (c_int, [c_int] * 7),

@@ -6,9 +6,9 @@ namespace lq2 {
 int w4_pack_launch(const int8_t*, int, int32_t*, int, int, cudaStream_t);
 size_t w4a16_stream_workspace_bytes(int, int, int);
 int w4a16_stream_launch(const __half*, int64_t, const int32_t*, const __half*, const __half*, __half*,
-                        int, int, int, int, void*, size_t, cudaStream_t);
+                        int, int, int, int, int, void*, size_t, cudaStream_t);
 int w4a16_umma_launch(const __half*, int64_t, const int32_t*, const __half*, const __half*, __half*, int, int,
-                      int, int, cudaStream_t);
+                      int, int, int, cudaStream_t);
 int kv4_store_launch(const __half*, const __half*, int64_t, int64_t, uint32_t*, const __half*, uint32_t*,
                      __half*, const int32_t*, int, int, int, int, int64_t, cudaStream_t);
 int kv4_materialize_launch(const uint32_t*, const __half*, const uint32_t*, const __half*, const int64_t*,
@@ -87,9 +87,10 @@ size_t lq2_w4a16_workspace_bytes(int m, int n, int k) {
     return w4a16_stream_workspace_bytes(m, n, k);
 }
 
-int lq2_w4a16_linear(const void* x, int64_t x_row_stride, const int32_t* packed, const void* scales,
-                     const void* zeros, void* y, int m, int n, int k, int group, void* workspace,
-                     size_t workspace_bytes, void* stream) {
+namespace {
+int w4a16_dispatch(const void* x, int64_t x_row_stride, const int32_t* packed, const void* scales,
+                   const void* zeros, void* y, int m, int n, int k, int group, int silu, void* workspace,
+                   size_t workspace_bytes, void* stream) {
     if (!x || !packed || !scales || !y) return LQ2_ERR_ARG;
     if (!w4_shape_ok(m, n, k, group)) return m <= 0 || n <= 0 || k <= 0 ? LQ2_ERR_ARG : LQ2_ERR_SHAPE;
     if (!aligned(x, 16) || x_row_stride % 8 || x_row_stride < k || !aligned(packed, 16) ||
@@ -99,11 +100,27 @@ int lq2_w4a16_linear(const void* x, int64_t x_row_stride, const int32_t* packed,
     if (m > 8)
         return w4a16_umma_launch(static_cast<const __half*>(x), x_row_stride, packed,
                                  static_cast<const __half*>(scales), static_cast<const __half*>(zeros),
-                                 static_cast<__half*>(y), m, n, k, group, static_cast<cudaStream_t>(stream));
+                                 static_cast<__half*>(y), m, n, k, group, silu, static_cast<cudaStream_t>(stream));
     return w4a16_stream_launch(static_cast<const __half*>(x), x_row_stride, packed,
                                static_cast<const __half*>(scales), static_cast<const __half*>(zeros),
-                               static_cast<__half*>(y), m, n, k, group, workspace, workspace_bytes,
+                               static_cast<__half*>(y), m, n, k, group, silu, workspace, workspace_bytes,
                                static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
+int lq2_w4a16_linear(const void* x, int64_t x_row_stride, const int32_t* packed, const void* scales,
+                     const void* zeros, void* y, int m, int n, int k, int group, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+    return w4a16_dispatch(x, x_row_stride, packed, scales, zeros, y, m, n, k, group, 0, workspace, workspace_bytes,
+                          stream);
+}
+
+int lq2_w4a16_gate_up_silu(const void* x, int64_t x_row_stride, const int32_t* packed, const void* scales,
+                           const void* zeros, void* y, int m, int n, int k, int group, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+    if (n % 64) return n > 0 ? LQ2_ERR_SHAPE : LQ2_ERR_ARG;
+    return w4a16_dispatch(x, x_row_stride, packed, scales, zeros, y, m, n, k, group, 1, workspace, workspace_bytes,
+                          stream);
 }
 
 int lq2_kv4_store(const void* k, const void* v, int64_t k_stride, int64_t v_stride, uint32_t* kq,

@@ -92,6 +92,21 @@ __device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
+// fp16(silu(fp32(g))) * u on a pair of fp16 values: F.silu(gate) * up of Qwen3MLP.forward
+// (qslab/runtime/model/qwen3.py:64) with torch's rounding points.
+__device__ __forceinline__ __half2 silu_mul2(__half2 g, __half2 u) {
+    const float2 a = __half22float2(g);
+    const __half2 s = __floats2half2_rn(a.x / (1.0f + expf(-a.x)), a.y / (1.0f + expf(-a.y)));
+    return __hmul2(s, u);
+}
+// The same applied to the fp32 sums of four gate and four up channels (rounded to fp16 first,
+// as the unfused projection would have stored them).
+__device__ __forceinline__ uint2 silu_mul_quad(const float4& g, const float4& u) {
+    const __half2 lo = silu_mul2(__floats2half2_rn(g.x, g.y), __floats2half2_rn(u.x, u.y));
+    const __half2 hi = silu_mul2(__floats2half2_rn(g.z, g.w), __floats2half2_rn(u.z, u.w));
+    return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
 // Streaming 128-bit / 64-bit global loads: the data is read once, keep it out of L1.
 __device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
     uint4 v;

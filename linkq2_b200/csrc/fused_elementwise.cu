@@ -108,11 +108,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __half* __restrict_
     const __half2* u = reinterpret_cast<const __half2*>(&ur);
     __half2 o[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 a = __half22float2(g[i]);
-        const __half2 s = __floats2half2_rn(a.x / (1.0f + expf(-a.x)), a.y / (1.0f + expf(-a.y)));
-        o[i] = __hmul2(s, u[i]);
-    }
+    for (int i = 0; i < 4; ++i) o[i] = silu_mul2(g[i], u[i]);
     *reinterpret_cast<uint4*>(out + (int64_t(row) * chunks + c) * 8) = *reinterpret_cast<uint4*>(o);
 }
 

@@ -66,6 +66,7 @@ struct W4Params {
     int m, n, k, group;
     int stages_per_rank;
     int early_weights;    // request weight bytes before the previous kernel of the stream has finished
+    int silu;             // columns are interleaved [4 gate | 4 up]: write silu(gate) * up, N / 2 wide
 };
 
 // ---- mbarrier / bulk-copy primitives (shared::cta addresses as 32-bit values)
@@ -349,6 +350,28 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
 
     // ---- write-out.  Consumer lane (g, t) owns columns n0..n0+3 of rows m0 + 8j + 2t (+1).
     if (ranks == 1) {
+        if (p.silu) {
+            // lane groups with even g hold four gate channels, their neighbours (g + 1) the matching
+            // four up channels: fetch those with a shuffle, then the even groups write
+            if (warp < CONSUMERS) {
+#pragma unroll
+                for (int j = 0; j < NJW; ++j) {
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        const float4 mine = make_float4(acc[0][j][r], acc[0][j][2 + r], acc[1][j][r], acc[1][j][2 + r]);
+                        float4 up;
+                        up.x = __shfl_xor_sync(0xffffffffu, mine.x, 4);
+                        up.y = __shfl_xor_sync(0xffffffffu, mine.y, 4);
+                        up.z = __shfl_xor_sync(0xffffffffu, mine.z, 4);
+                        up.w = __shfl_xor_sync(0xffffffffu, mine.w, 4);
+                        const int m = m0 + 8 * (jpart * NJW + j) + 2 * t + r;
+                        if (n_ok && (g & 1) == 0 && m < p.m)
+                            *reinterpret_cast<uint2*>(p.y + int64_t(m) * (p.n / 2) + n0 / 2) = silu_mul_quad(mine, up);
+                    }
+                }
+            }
+            return;
+        }
         if (n_ok) {
 #pragma unroll
             for (int j = 0; j < NJW; ++j) {
@@ -392,15 +415,28 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
     }
     asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
     asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-    {
+    auto slice_sum = [&](int ml, int col) {
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < ranks; ++q) {
+            const float4 v = *reinterpret_cast<const float4*>(recv + (size_t(q) * MT + ml) * W + col);
+            sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+        }
+        return sum;
+    };
+    if (p.silu) {
+        const int octs = W / 8;                            // [4 gate | 4 up] blocks of my slice
+        for (int e = tid; e < rows * octs; e += L::THREADS) {
+            const int ml = e / octs, col = (e - ml * octs) * 8;
+            const int nn = tile_n0 + rank * W + col;
+            if (nn < p.n)
+                *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * (p.n / 2) + nn / 2) =
+                    silu_mul_quad(slice_sum(ml, col), slice_sum(ml, col + 4));
+        }
+    } else {
         const int quads = W / 4;
         for (int e = tid; e < rows * quads; e += L::THREADS) {
             const int ml = e / quads, col = (e - ml * quads) * 4;
-            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int q = 0; q < ranks; ++q) {
-                const float4 v = *reinterpret_cast<const float4*>(recv + (size_t(q) * MT + ml) * W + col);
-                sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-            }
+            const float4 sum = slice_sum(ml, col);
             const int nn = tile_n0 + rank * W + col;
             if (nn < p.n) {
                 const __half2 lo = __floats2half2_rn(sum.x, sum.y);
@@ -536,7 +572,7 @@ int launch_z(const W4Params& p, const Plan& pl, cudaStream_t st) {
 size_t w4a16_stream_workspace_bytes(int, int, int) { return 0; }
 
 int w4a16_stream_launch(const __half* x, int64_t ldx, const int32_t* packed, const __half* scales,
-                        const __half* zeros, __half* y, int m, int n, int k, int group,
+                        const __half* zeros, __half* y, int m, int n, int k, int group, int silu,
                         void*, size_t, cudaStream_t st) {
     const Plan pl = make_plan(m, n, k);
     if (pl.m_tiles > 65535) return LQ2_ERR_SHAPE;
@@ -545,6 +581,7 @@ int w4a16_stream_launch(const __half* x, int64_t ldx, const int32_t* packed, con
     p.m = m; p.n = n; p.k = k; p.group = group;
     p.stages_per_rank = pl.spr;
     p.early_weights = early_weight_fetch() ? 1 : 0;
+    p.silu = silu;
     switch (pl.nj) {
         case 1: return launch_z<1>(p, pl, st);
         case 2: return launch_z<2>(p, pl, st);

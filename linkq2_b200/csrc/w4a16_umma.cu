@@ -63,6 +63,7 @@ struct UParams {
     int m, n, k, group;
     int stages_per_rank;
     int early_weights;    // request weight bytes before the previous kernel of the stream has finished
+    int silu;             // columns are interleaved [4 gate | 4 up]: write silu(gate) * up, N / 2 wide
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -489,19 +490,34 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             cluster_wait_acquire();
         }
         LQ2_STAMP(5, threadIdx.x == 0);                                // all parts of my slice have arrived
-        const int quads = W / 4;
-        for (int e = tid; e < rows * quads; e += kUThreads) {
-            const int ml = e / quads, col = (e - ml * quads) * 4;
+        auto slice_sum = [&](int ml, int col) {
             float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int q = 0; q < ranks; ++q) {
                 const float4 v = *reinterpret_cast<const float4*>(recv + (size_t(q) * MB + ml) * W + col);
                 sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
             }
-            const int nn = tile_n0 + rank * W + col;
-            if (nn < p.n) {
-                const __half2 lo = __floats2half2_rn(sum.x, sum.y);
-                const __half2 hi = __floats2half2_rn(sum.z, sum.w);
-                *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * p.n + nn) = make_uint2(h2_as_u32(lo), h2_as_u32(hi));
+            return sum;
+        };
+        if (p.silu) {
+            const int octs = W / 8;                        // [4 gate | 4 up] blocks of my slice
+            for (int e = tid; e < rows * octs; e += kUThreads) {
+                const int ml = e / octs, col = (e - ml * octs) * 8;
+                const int nn = tile_n0 + rank * W + col;
+                if (nn < p.n)
+                    *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * (p.n / 2) + nn / 2) =
+                        silu_mul_quad(slice_sum(ml, col), slice_sum(ml, col + 4));
+            }
+        } else {
+            const int quads = W / 4;
+            for (int e = tid; e < rows * quads; e += kUThreads) {
+                const int ml = e / quads, col = (e - ml * quads) * 4;
+                const float4 sum = slice_sum(ml, col);
+                const int nn = tile_n0 + rank * W + col;
+                if (nn < p.n) {
+                    const __half2 lo = __floats2half2_rn(sum.x, sum.y);
+                    const __half2 hi = __floats2half2_rn(sum.z, sum.w);
+                    *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * p.n + nn) = make_uint2(h2_as_u32(lo), h2_as_u32(hi));
+                }
             }
         }
         LQ2_STAMP(6, threadIdx.x == 0);                                // output written
@@ -534,19 +550,34 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             constexpr int QUADS = kUM / 4;
             const int q0 = rank * QUADS / ranks, q1 = (rank + 1) * QUADS / ranks;
             const int quads = q1 - q0;
-            for (int e = tid; e < rows * quads; e += kUThreads) {
-                const int ml = e / quads, col = (q0 + e % quads) * 4;
+            auto tile_sum = [&](int ml, int col) {
                 float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
                 for (int q = 0; q < ranks; ++q) {
                     const float* src = ranks > 1 ? cluster.map_shared_rank(red, q) : red;
                     const float4 v = *reinterpret_cast<const float4*>(src + ml * kUM + col);
                     sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
                 }
-                const int nn = tile_n0 + col;
-                if (nn < p.n) {
-                    const __half2 lo = __floats2half2_rn(sum.x, sum.y);
-                    const __half2 hi = __floats2half2_rn(sum.z, sum.w);
-                    *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * p.n + nn) = make_uint2(h2_as_u32(lo), h2_as_u32(hi));
+                return sum;
+            };
+            if (p.silu) {                                  // q0 is even for every power-of-two cluster size
+                const int octs = quads / 2;
+                for (int e = tid; e < rows * octs; e += kUThreads) {
+                    const int ml = e / octs, col = (q0 + 2 * (e % octs)) * 4;
+                    const int nn = tile_n0 + col;
+                    if (nn < p.n)
+                        *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * (p.n / 2) + nn / 2) =
+                            silu_mul_quad(tile_sum(ml, col), tile_sum(ml, col + 4));
+                }
+            } else {
+                for (int e = tid; e < rows * quads; e += kUThreads) {
+                    const int ml = e / quads, col = (q0 + e % quads) * 4;
+                    const float4 sum = tile_sum(ml, col);
+                    const int nn = tile_n0 + col;
+                    if (nn < p.n) {
+                        const __half2 lo = __floats2half2_rn(sum.x, sum.y);
+                        const __half2 hi = __floats2half2_rn(sum.z, sum.w);
+                        *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * p.n + nn) = make_uint2(h2_as_u32(lo), h2_as_u32(hi));
+                    }
                 }
             }
         }
@@ -672,12 +703,13 @@ int launch_umma_z(const __half* x, int64_t ldx, const int32_t* packed, const __h
 }  // namespace
 
 int w4a16_umma_launch(const __half* x, int64_t ldx, const int32_t* packed, const __half* scales,
-                      const __half* zeros, __half* y, int m, int n, int k, int group, cudaStream_t st) {
+                      const __half* zeros, __half* y, int m, int n, int k, int group, int silu, cudaStream_t st) {
     const UPlan pl = make_uplan(m, n, k);
     if (pl.m_tiles > 65535) return LQ2_ERR_SHAPE;
     UParams p;
     p.y = y; p.m = m; p.n = n; p.k = k; p.group = group; p.stages_per_rank = pl.spr;
     p.early_weights = early_weight_fetch() ? 1 : 0;
+    p.silu = silu;
     switch (pl.mb) {
         case 16: return launch_umma_z<16>(x, ldx, packed, scales, zeros, p, pl, st);
         case 32: return launch_umma_z<32>(x, ldx, packed, scales, zeros, p, pl, st);

@@ -17,7 +17,7 @@ def set_constant_weights(enabled: bool) -> bool:
 
 
 def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
-           meta) -> torch.Tensor:
+           meta, *, gate_up_silu: bool = False) -> torch.Tensor:
     """``x [..., K] fp16`` times the dequantised ``[K, N]`` weight -> ``[..., N] fp16``.
 
     ``packed [K/8, N] int32``, ``scales [K/G, N] fp16``; ``zeros`` is either the
@@ -26,6 +26,11 @@ def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: t
     reference (``triton_kernels/gemv_revsplitK_A16fWnO16f_int32packing.py:376``).
     ``meta`` is the 12-tuple built by ``from_quantized``; only its bit width,
     group size and group mode are read.
+
+    ``gate_up_silu`` (no counterpart in the reference's signature): the buffers hold a
+    gate and an up projection with their columns interleaved in blocks of four
+    (``B200Linear.fuse_gate_up``); the result is ``silu(gate(x)) * up(x)``, ``N / 2`` wide
+    (``lq2_w4a16_gate_up_silu``).
     """
     if meta[0] != 4 or meta[9] != 3:
         raise ValueError("only 4-bit weights with (u - zero) * scale dequantisation are supported")
@@ -38,12 +43,15 @@ def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: t
     k = k8 * 8
     if x.shape[-1] != k:
         raise ValueError(f"expected input width {k}, got {x.shape[-1]}")
-    shape = x.shape[:-1] + (n,)
+    if gate_up_silu and n % 64:
+        raise ValueError("gate_up_silu needs a multiple of 64 fused columns")
+    n_out = n // 2 if gate_up_silu else n
+    shape = x.shape[:-1] + (n_out,)
     x2 = x.reshape(-1, k)
     if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
         x2 = x2.contiguous()
     m = x2.shape[0]
-    y = torch.empty((m, n), dtype=torch.float16, device=x.device)
+    y = torch.empty((m, n_out), dtype=torch.float16, device=x.device)
     if m == 0:
         return y.view(shape)
     zero_ptr = None if zeros.numel() == 1 else zeros.data_ptr()
@@ -51,9 +59,10 @@ def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: t
         need = _lib.lib.lq2_w4a16_workspace_bytes(m, n, k)
         ws = _workspace.get("w4a16", need, x.device) if need else None
         stream = torch.cuda.current_stream().cuda_stream
-        status = _lib.lib.lq2_w4a16_linear(
+        entry = _lib.lib.lq2_w4a16_gate_up_silu if gate_up_silu else _lib.lib.lq2_w4a16_linear
+        status = entry(
             x2.data_ptr(), x2.stride(0), packed.data_ptr(), scales.data_ptr(), zero_ptr, y.data_ptr(),
             m, n, k, group, ws.data_ptr() if need else None, ws.numel() if need else 0, stream)
-    _lib.check(status, "lq2_w4a16_linear")
+    _lib.check(status, "lq2_w4a16_gate_up_silu" if gate_up_silu else "lq2_w4a16_linear")
     _lib.count()
     return y.view(shape)

@@ -84,7 +84,36 @@ class B200Linear(QuantLinear):
         _weights_complete(fused.packed.device)
         return fused
 
+    @classmethod
+    @torch.no_grad()
+    def fuse_gate_up(cls, gate, up):
+        """One layer computing ``silu(gate(x)) * up(x)`` in a single launch: the columns of
+        the two projections are interleaved in blocks of four, ``[g0..g3 | u0..u3 | g4..``,
+        so that every output tile of the kernel holds matching gate and up channels and its
+        epilogue can apply the activation (``lq2_w4a16_gate_up_silu``).  Same conditions as
+        ``fuse_columns``; ``out_features`` is the intermediate size."""
+        fused = cls.fuse_columns([gate, up])
+        n = gate.out_features
+        if up.out_features != n or n % 32:
+            raise ValueError("gate and up projections must have the same width, a multiple of 32")
+
+        def interleave(a, b):
+            rows = a.shape[0]
+            return torch.stack([a.view(rows, n // 4, 4), b.view(rows, n // 4, 4)], dim=2).reshape(rows, 2 * n)
+        fused.packed = interleave(gate.packed, up.packed).contiguous()
+        fused.scales = interleave(gate.scales, up.scales).contiguous()
+        if gate.zeros.numel() > 1:
+            fused.zeros = interleave(gate.zeros, up.zeros).contiguous()
+        fused.out_features = n
+        fused.gate_up_silu = True
+        _weights_complete(fused.packed.device)
+        return fused
+
     def forward(self, x):
+        if getattr(self, "gate_up_silu", False):
+            if x.dtype != self.compute_dtype:
+                raise TypeError(f"expected {self.compute_dtype}, got {x.dtype}")
+            return linear(x, self.packed, self.scales, self.zeros, self._meta, gate_up_silu=True)
         if x.dtype != self.compute_dtype:
             raise TypeError(f"expected {self.compute_dtype}, got {x.dtype}")
         if self.input_scale is not None:

@@ -10,6 +10,7 @@ all-reduced.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -60,13 +61,16 @@ class ModelConfig:
                    tie_word_embeddings=True)
 
 
-def _fuse(layers):
+def _fuse(layers, gate_up=False):
     """Fused W4 projection for layers sharing their input, or None when they are
     not packed W4 layers or carry AWQ input scales (the reason the reference keeps
-    them apart, ``qslab/runtime/model/qwen3.py:3-5``)."""
+    them apart, ``qslab/runtime/model/qwen3.py:3-5``).  ``gate_up``: the pair is fused
+    together with the SiLU * up that follows it."""
     from linkq2_b200.runtime.backends.b200 import B200Linear
     if not all(isinstance(l, B200Linear) and l.input_scale is None for l in layers):
         return None
+    if gate_up and layers[0].out_features % 32 == 0 and os.environ.get("LQ2_FUSE_SILU", "1") != "0":
+        return B200Linear.fuse_gate_up(*layers)
     return B200Linear.fuse_columns(layers)
 
 
@@ -131,17 +135,20 @@ class Qwen3MLP(nn.Module):
         self.gate_up_proj = None
 
     def fuse(self):
-        """Replace gate/up by one projection when the checkpoint allows it."""
-        self.gate_up_proj = _fuse([self.gate_proj, self.up_proj])
+        """Replace gate/up by one projection with the activation in its epilogue when the
+        checkpoint allows it."""
+        self.gate_up_proj = _fuse([self.gate_proj, self.up_proj], gate_up=True)
         if self.gate_up_proj is not None:
             self.gate_proj = self.up_proj = None
 
     def forward(self, x):
-        if self.gate_up_proj is not None:
-            gate, up = self.gate_up_proj(x).chunk(2, dim=-1)
+        if self.gate_up_proj is not None and getattr(self.gate_up_proj, "gate_up_silu", False):
+            hidden = self.gate_up_proj(x)                   # silu(gate(x)) * up(x)
+        elif self.gate_up_proj is not None:
+            hidden = silu_mul(*self.gate_up_proj(x).chunk(2, dim=-1))
         else:
-            gate, up = self.gate_proj(x), self.up_proj(x)
-        return self.tp.reduce_or_defer(self.down_proj(silu_mul(gate, up)))
+            hidden = silu_mul(self.gate_proj(x), self.up_proj(x))
+        return self.tp.reduce_or_defer(self.down_proj(hidden))
 
 
 class Qwen3DecoderLayer(nn.Module):

@@ -182,3 +182,36 @@ def test_buffers_move_and_release():
     gc.collect()
     torch.cuda.synchronize()
     assert torch.cuda.memory_allocated() == baseline
+
+
+@pytest.mark.parametrize("affine", [False, True])
+@pytest.mark.parametrize("k,n", [(256, 128), (4096, 12288), (4096, 1536), (1024, 6144)])
+def test_gate_up_with_silu_epilogue_is_bit_identical(k, n, affine):
+    """``fuse_gate_up`` (columns interleaved in blocks of four, activation in the kernel's
+    epilogue) returns the bits of ``silu_mul`` applied to the plainly concatenated projection
+    (same shape, hence the same K split and summation order) for every routed kernel:
+    weight-streaming (M <= 8), tcgen05 with pushed reduction (M <= 64) and with pulled
+    (M > 64); against the two separate projections, whose K split may differ, it agrees to
+    fp16 rounding of the sums."""
+    from linkq2_b200.kernels.fused import silu_mul
+    from linkq2_b200.runtime.backends.b200 import B200Linear
+    layers = []
+    for seed in (11, 12):
+        w = ow.seeded_weight(n, k, seed=seed + n)
+        if affine:
+            values, scale, zero = ow.affine_quantize(w, 128)
+        else:
+            (values, scale), zero = ow.rtn_quantize(w, 128), None
+        layers.append(make_layer(values, scale, zero, 128, not affine))
+    gate, up = layers
+    fused = B200Linear.fuse_gate_up(gate, up)
+    plain = B200Linear.fuse_columns([gate, up])
+    assert fused.out_features == n and fused.packed.shape == (k // 8, 2 * n)
+    for m in (1, 5, 8, 9, 32, 64, 65, 200):
+        x = ow.seeded_activation(m, k, seed=m, outliers=True).cuda()
+        got = fused(x)
+        assert got.shape == (m, n)
+        want = silu_mul(*plain(x).chunk(2, dim=-1))
+        assert torch.equal(got, want), (m, (got.float() - want.float()).abs().max().item())
+        apart = silu_mul(gate(x), up(x)).float()
+        assert ((got.float() - apart).abs() <= 4e-3 * apart.abs() + 1e-3).all()

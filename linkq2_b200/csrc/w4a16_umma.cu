@@ -340,7 +340,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             if (lane == 0) {
                 const uint32_t a_tmem = tmem_base + L::ACC_COLS + aslot * L::A_COLS;
                 const uint32_t xbase = smem_u32(r_ring + rslot * L::R_STAGE_BYTES);
-#ifndef LQ2_U_SKIP_MMA
 #pragma unroll
                 for (int kk = 0; kk < UK / 16; ++kk) {
                     // a K step of 16 fp16: 8 TMEM columns of A, 32 bytes inside the swizzled rows of B
@@ -349,7 +348,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                                 smem_desc_sw128(xbase + (kk >> 2) * L::XBOX_BYTES + (kk & 3) * 32), idesc,
                                 (it > 0 || kk > 0) ? 1u : 0u);
                 }
-#endif
                 umma_commit(a_free(aslot));                   // both buffers are reusable once these MMAs are done
                 umma_commit(raw_free(rslot));
                 if (it == my_stages - 1) umma_commit(acc_full);
@@ -427,16 +425,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                     cols[4 * r4 + 1] = __byte_perm(v26, v37, 0x5410);        // k2 k3
                     cols[4 * r4 + 2] = __byte_perm(v04, v15, 0x7632);        // k4 k5
                     cols[4 * r4 + 3] = __byte_perm(v26, v37, 0x7632);        // k6 k7
-#ifdef LQ2_U_SKIP_ALU
-                    cols[4 * r4 + 0] = w; cols[4 * r4 + 1] = w8; cols[4 * r4 + 2] = w; cols[4 * r4 + 3] = w8;
-#endif
-#ifdef LQ2_U_SUBNORMAL_PROBE
-                    // raw codes as fp16 subnormals u * 2^-24, natural k order, no scale, no zero point
-                    cols[4 * r4 + 0] = (w & 0xfu) | ((w & 0xf0u) << 12);
-                    cols[4 * r4 + 1] = ((w >> 8) & 0xfu) | (((w >> 8) & 0xf0u) << 12);
-                    cols[4 * r4 + 2] = ((w >> 16) & 0xfu) | (((w >> 16) & 0xf0u) << 12);
-                    cols[4 * r4 + 3] = ((w >> 24) & 0xfu) | (((w >> 24) & 0xf0u) << 12);
-#endif
                 }
                 tmem_st16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + aslot * L::A_COLS +
                               khalf * (UK / 4) + 16 * b, cols);

@@ -225,6 +225,65 @@ class ModelRunner:
         self.graph_replays += 1
         return graphs.families[1].buffers['outputs'][:b]
 
+    @torch.inference_mode()
+    def run_steps(self, seqs: list[Sequence], steps: int) -> list[list[int]]:
+        """``steps`` greedy decode steps in a row without a host round trip between them
+        (multi-step decoding): the token ids of step i+1 are taken from step i's arg-max on
+        the device, every step's positions, slots and context lengths are known in advance,
+        and the tokens come back through one pinned buffer, read once at the end.  Per step
+        there is still one host-to-device copy of the step's record and one device-to-host
+        copy of its tokens.  Appends the tokens to the sequences and returns them per step.
+        The block tables must already cover ``len(seq) + steps`` positions."""
+        graphs = self.cuda_graphs
+        b = len(seqs)
+        if graphs is None or b > max(graphs.batch_sizes):
+            out = []
+            for _ in range(steps):
+                tokens = self.run(seqs, False)
+                for seq, tok in zip(seqs, tokens):
+                    seq.append(tok)
+                out.append(tokens)
+            return out
+        import numpy as np
+        width = max(len(seq.block_table) for seq in seqs)
+        for seq in seqs:
+            if (len(seq) + steps - 1) // self.block_size >= len(seq.block_table):
+                raise ValueError("run_steps needs block tables that cover every new position")
+        n = 4 * b + b * width
+        records = torch.empty(steps, n, dtype=torch.int32, pin_memory=True)
+        rec = records.numpy()
+        base = np.array([len(seq) for seq in seqs], dtype=np.int64)
+        tables = np.full((b, width), -1, dtype=np.int32)
+        for i, seq in enumerate(seqs):
+            tables[i, :len(seq.block_table)] = seq.block_table
+        bs = self.block_size
+        for i in range(steps):
+            pos = base - 1 + i
+            rec[i, 0:b] = [seq.last_token for seq in seqs] if i == 0 else 0
+            rec[i, b:2 * b] = pos
+            rec[i, 2 * b:3 * b] = tables[np.arange(b), pos // bs] * bs + pos % bs
+            rec[i, 3 * b:4 * b] = base + i
+            rec[i, 4 * b:] = tables.reshape(-1)
+        staged = torch.empty(steps, n, dtype=torch.int32, device=self.device)
+        tokens_host = torch.empty(steps, b, dtype=torch.int64, pin_memory=True)
+        ids = None
+        for i in range(steps):
+            staged[i].copy_(records[i], non_blocking=True)
+            if ids is not None:
+                staged[i, :b] = ids
+            bucket = graphs.stage_packed(staged[i], b, width)
+            graphs.run_graph(1, bucket)
+            self.graph_replays += 1
+            self.last_logits = self.model.compute_logits(graphs.families[1].buffers['outputs'][:b])
+            ids = self.last_logits.argmax(dim=-1)
+            tokens_host[i].copy_(ids, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        out = tokens_host.tolist()
+        for row in out:
+            for seq, tok in zip(seqs, row):
+                seq.append(tok)
+        return out
+
     def _finish(self, seqs, hidden, is_prefill, counts):
         if is_prefill:
             hidden = hidden[(get_context().cu_seqlens_q[1:] - 1).long()]

@@ -190,3 +190,31 @@ def test_packed_decode_staging_equals_the_seven_copies(tmp_path):
             if name in ("input_ids", "positions"):             # rows beyond the batch are never read
                 got, want = got[:batch], want[:batch]
             assert torch.equal(got, want), name
+
+
+def test_multi_step_decoding_equals_step_by_step(tmp_path):
+    """``run_steps`` (token ids fed back on the device, one host synchronisation per call)
+    decodes the same tokens as ``run`` called once per step, and both equal the oracle."""
+    from linkq2_b200.runtime.model.qwen3 import ModelConfig
+    from linkq2_b200.runtime.state import BlockPool, Sequence
+    weights = write_checkpoint(tmp_path / "w4")
+    runner = make_runner(tmp_path / "w4", eager=False)
+    g = torch.Generator().manual_seed(21)
+    prompts = [torch.randint(0, 127, (n,), generator=g).tolist() for n in (12, 30, 5)]
+    step_by_step, _ = generate(runner, prompts, 40, 1000)
+    pool = BlockPool(16, shuffle_seed=5)
+    seqs = [Sequence(p, 128) for p in prompts]
+    for s in seqs:
+        pool.ensure(s, len(s) + 60)
+    first = runner.run(seqs, True)
+    for s, t in zip(seqs, first):
+        s.append(t)
+    rows = runner.run_steps(seqs, 13) + runner.run_steps(seqs, 26)
+    got = [[first[i]] + [row[i] for row in rows] for i in range(len(prompts))]
+    assert got == step_by_step
+    assert [s.token_ids[len(p):] for s, p in zip(seqs, prompts)] == got
+    cfg = ModelConfig.from_dict(CFG)
+    oracle = oq.OracleQwen3(cfg, weights, kscale=torch.full((2, 1, 64), 0.3), max_tokens=512)
+    assert got[0] == oracle.greedy(prompts[0], 40, chunk=len(prompts[0]))
+    with pytest.raises(ValueError):
+        runner.run_steps(seqs, 500)                         # beyond the allocated blocks

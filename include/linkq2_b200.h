@@ -329,6 +329,23 @@ int lq2_rmsnorm_allreduce(const void* x, int64_t x_row_stride, const void* resid
                           void* residual_out, int rows, int hidden, float eps, void* const* buffers, int rank,
                           int world, size_t max_message_bytes, void* stream);
 
+/*
+ * The producer side of the same exchange fused into the projection: lq2_w4a16_linear for a
+ * row-split o_proj / down_proj (8 < M <= 64, else LQ2_ERR_SHAPE) whose epilogue, besides writing
+ * this rank's partial sum to y, stores every finished group of four outputs directly into the
+ * peers' exchange buffers in the flagged form lq2_rmsnorm_allreduce gathers, so the transfer
+ * over NVLink runs while the rest of the projection is still being computed.  It must be
+ * followed, as the next exchange call on every rank, by lq2_rmsnorm_allreduce_pushed on y:
+ * the same as lq2_rmsnorm_allreduce except that it only gathers (nothing is sent again).
+ * M * N * 2 must not exceed max_message_bytes (LQ2_ERR_LIMIT).
+ */
+int lq2_w4a16_linear_push(const void* x, int64_t x_row_stride, const int32_t* packed, const void* scales,
+                          const void* zeros, void* y, int m, int n, int k, int group, void* const* buffers, int rank,
+                          int world, size_t max_message_bytes, void* stream);
+int lq2_rmsnorm_allreduce_pushed(const void* x, int64_t x_row_stride, const void* residual, const void* weight,
+                                 void* out, void* residual_out, int rows, int hidden, float eps, void* const* buffers,
+                                 int rank, int world, size_t max_message_bytes, void* stream);
+
 /* Number of abandoned waits on the current device since the library was loaded
  * (synchronises the device); 0 in a healthy run. */
 unsigned int lq2_allreduce_timeouts(void);

@@ -28,6 +28,10 @@ SIGNATURES = {
     "lq2_allreduce_fp16": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int, c_size_t, c_void_p]),
     "lq2_rmsnorm_allreduce": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                       c_float, c_void_p, c_int, c_int, c_size_t, c_void_p]),
+    "lq2_rmsnorm_allreduce_pushed": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                             c_float, c_void_p, c_int, c_int, c_size_t, c_void_p]),
+    "lq2_w4a16_linear_push": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                      c_int, c_void_p, c_int, c_int, c_size_t, c_void_p]),
     "lq2_allreduce_timeouts": (c_uint, []),
     "lq2_w4a16_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "lq2_w4a16_linear": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -8,7 +8,7 @@ size_t w4a16_stream_workspace_bytes(int, int, int);
 int w4a16_stream_launch(const __half*, int64_t, const int32_t*, const __half*, const __half*, __half*,
                         int, int, int, int, int, void*, size_t, cudaStream_t);
 int w4a16_umma_launch(const __half*, int64_t, const int32_t*, const __half*, const __half*, __half*, int, int,
-                      int, int, int, cudaStream_t);
+                      int, int, int, const PushTarget*, cudaStream_t);
 int kv4_store_launch(const __half*, const __half*, int64_t, int64_t, uint32_t*, const __half*, uint32_t*,
                      __half*, const int32_t*, int, int, int, int, int64_t, cudaStream_t);
 int kv4_materialize_launch(const uint32_t*, const __half*, const uint32_t*, const __half*, const int64_t*,
@@ -90,17 +90,19 @@ size_t lq2_w4a16_workspace_bytes(int m, int n, int k) {
 namespace {
 int w4a16_dispatch(const void* x, int64_t x_row_stride, const int32_t* packed, const void* scales,
                    const void* zeros, void* y, int m, int n, int k, int group, int silu, void* workspace,
-                   size_t workspace_bytes, void* stream) {
+                   size_t workspace_bytes, void* stream, const PushTarget* push = nullptr) {
     if (!x || !packed || !scales || !y) return LQ2_ERR_ARG;
     if (!w4_shape_ok(m, n, k, group)) return m <= 0 || n <= 0 || k <= 0 ? LQ2_ERR_ARG : LQ2_ERR_SHAPE;
     if (!aligned(x, 16) || x_row_stride % 8 || x_row_stride < k || !aligned(packed, 16) ||
         !aligned(scales, 16) || (zeros && !aligned(zeros, 16)) || !aligned(y, 8))
         return LQ2_ERR_ALIGN;
     // up to 8 rows: the weight-streaming kernel; beyond that the tcgen05 kernel
+    if (push && (m <= 8 || m > 64)) return LQ2_ERR_SHAPE;
     if (m > 8)
         return w4a16_umma_launch(static_cast<const __half*>(x), x_row_stride, packed,
                                  static_cast<const __half*>(scales), static_cast<const __half*>(zeros),
-                                 static_cast<__half*>(y), m, n, k, group, silu, static_cast<cudaStream_t>(stream));
+                                 static_cast<__half*>(y), m, n, k, group, silu, push,
+                                 static_cast<cudaStream_t>(stream));
     return w4a16_stream_launch(static_cast<const __half*>(x), x_row_stride, packed,
                                static_cast<const __half*>(scales), static_cast<const __half*>(zeros),
                                static_cast<__half*>(y), m, n, k, group, silu, workspace, workspace_bytes,
@@ -113,6 +115,23 @@ int lq2_w4a16_linear(const void* x, int64_t x_row_stride, const int32_t* packed,
                      size_t workspace_bytes, void* stream) {
     return w4a16_dispatch(x, x_row_stride, packed, scales, zeros, y, m, n, k, group, 0, workspace, workspace_bytes,
                           stream);
+}
+
+int lq2_w4a16_linear_push(const void* x, int64_t x_row_stride, const int32_t* packed, const void* scales,
+                          const void* zeros, void* y, int m, int n, int k, int group, void* const* buffers, int rank,
+                          int world, size_t max_message_bytes, void* stream) {
+    if (!buffers) return LQ2_ERR_ARG;
+    if (world < 2 || world > kMaxWorld || rank < 0 || rank >= world || max_message_bytes % 16) return LQ2_ERR_SHAPE;
+    if (m > 0 && n > 0 && size_t(m) * n * 2 > max_message_bytes) return LQ2_ERR_LIMIT;
+    PushTarget push;
+    for (int p = 0; p < kMaxWorld; ++p) {
+        push.peers.base[p] = p < world ? static_cast<unsigned char*>(buffers[p]) : nullptr;
+        if (p < world && !push.peers.base[p]) return LQ2_ERR_ARG;
+    }
+    push.rank = rank;
+    push.world = world;
+    push.max_bytes = max_message_bytes;
+    return w4a16_dispatch(x, x_row_stride, packed, scales, zeros, y, m, n, k, group, 0, nullptr, 0, stream, &push);
 }
 
 int lq2_w4a16_gate_up_silu(const void* x, int64_t x_row_stride, const int32_t* packed, const void* scales,

@@ -71,6 +71,27 @@ inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
     return cudaLaunchKernelEx(&cfg, kernel, KArgs(args)...) == cudaSuccess ? LQ2_OK : LQ2_ERR_CUDA;
 }
 
+// ---- layout of a rank's tensor-parallel exchange buffer (described in tp_allreduce.cu)
+constexpr int kMaxWorld = 8;
+constexpr int kMaxCtas = 256;
+struct PeerTable {
+    unsigned char* base[kMaxWorld];
+};
+// Where a projection kernel pushes its output for the all-reduce that follows it; world == 0: nowhere.
+struct PushTarget {
+    PeerTable peers;
+    int rank, world;
+    size_t max_bytes;
+};
+__host__ __device__ inline size_t flags_offset() { return 256; }
+__host__ __device__ inline size_t slots_offset(int world) {
+    const size_t raw = flags_offset() + size_t(2) * world * kMaxCtas * 4;
+    return (raw + 255) / 256 * 256;
+}
+__host__ __device__ inline size_t llslots_offset(int world, size_t max_bytes) {
+    return slots_offset(world) + size_t(2) * world * max_bytes;
+}
+
 // ---- warp-level tensor core op used as a dot-product engine by the
 // ---- bandwidth-bound kernels: D(16x8,f32) += A(16x16,f16) * B(16x8,f16)
 __device__ __forceinline__ void mma_m16n8k16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,

@@ -44,26 +44,11 @@ namespace lq2 {
 
 namespace {
 
-constexpr int kMaxWorld = 8;
-constexpr int kMaxCtas = 256;
 constexpr int kArThreads = 512;
 constexpr int kBytesPerCta = kArThreads * 16;          // one 128-bit access per thread and pass
 constexpr long long kMaxPolls = 1ll << 25;              // on the order of ten seconds of polling
 
-struct PeerTable {
-    unsigned char* base[kMaxWorld];
-};
-
 __device__ unsigned int g_lq2_allreduce_timeouts = 0;
-
-__host__ __device__ inline size_t flags_offset() { return 256; }
-__host__ __device__ inline size_t slots_offset(int world) {
-    const size_t raw = flags_offset() + size_t(2) * world * kMaxCtas * 4;
-    return (raw + 255) / 256 * 256;
-}
-__host__ __device__ inline size_t llslots_offset(int world, size_t max_bytes) {
-    return slots_offset(world) + size_t(2) * world * max_bytes;
-}
 
 __device__ __forceinline__ uint4 ld_volatile_u4(const void* p) {
     uint4 v;
@@ -185,7 +170,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
     const __half* x, int64_t x_stride, const __half* residual, const __half* __restrict__ weight, __half* out,
     __half* residual_out, const int hidden, const float eps, const PeerTable peers, const int rank,
-    const int world, const size_t max_bytes) {
+    const int world, const size_t max_bytes, const int pushed) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ float partial[kNormThreads / 32];
@@ -210,7 +195,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
             const uint4 lo = make_uint4(own[c].x, seq, own[c].y, seq), hi = make_uint4(own[c].z, seq, own[c].w, seq);
             const size_t off = ll + size_t(rank) * 2 * max_bytes + (size_t(row) * chunks + idx) * 32;
             for (int p = 0; p < world; ++p) {
-                if (p == rank) continue;
+                if (p == rank || pushed) continue;          // pushed: the producing kernel has sent it already
                 uint4* dst = reinterpret_cast<uint4*>(peers.base[p] + off);
                 dst[0] = lo;
                 dst[1] = hi;
@@ -371,9 +356,9 @@ int lq2_allreduce_fp16(const void* x, void* out, int64_t count, void* const* buf
                       max_message_bytes);
 }
 
-int lq2_rmsnorm_allreduce(const void* x, int64_t x_row_stride, const void* residual, const void* weight, void* out,
-                          void* residual_out, int rows, int hidden, float eps, void* const* buffers, int rank,
-                          int world, size_t max_message_bytes, void* stream) {
+static int rmsnorm_allreduce_impl(const void* x, int64_t x_row_stride, const void* residual, const void* weight,
+                                  void* out, void* residual_out, int rows, int hidden, float eps, void* const* buffers,
+                                  int rank, int world, size_t max_message_bytes, int pushed, void* stream) {
     if (rows == 0) return LQ2_OK;
     if (!x || !residual || !weight || !out || !residual_out || !buffers || rows < 0 || hidden <= 0) return LQ2_ERR_ARG;
     if (world < 2 || world > kMaxWorld || rank < 0 || rank >= world) return LQ2_ERR_SHAPE;
@@ -390,7 +375,21 @@ int lq2_rmsnorm_allreduce(const void* x, int64_t x_row_stride, const void* resid
     return launch_pdl(rmsnorm_allreduce_kernel, dim3(rows), dim3(kNormThreads), 0, static_cast<cudaStream_t>(stream), 1,
                       static_cast<const __half*>(x), x_row_stride, static_cast<const __half*>(residual),
                       static_cast<const __half*>(weight), static_cast<__half*>(out),
-                      static_cast<__half*>(residual_out), hidden, eps, peers, rank, world, max_message_bytes);
+                      static_cast<__half*>(residual_out), hidden, eps, peers, rank, world, max_message_bytes, pushed);
+}
+
+int lq2_rmsnorm_allreduce(const void* x, int64_t x_row_stride, const void* residual, const void* weight, void* out,
+                          void* residual_out, int rows, int hidden, float eps, void* const* buffers, int rank,
+                          int world, size_t max_message_bytes, void* stream) {
+    return rmsnorm_allreduce_impl(x, x_row_stride, residual, weight, out, residual_out, rows, hidden, eps, buffers, rank,
+                                  world, max_message_bytes, 0, stream);
+}
+
+int lq2_rmsnorm_allreduce_pushed(const void* x, int64_t x_row_stride, const void* residual, const void* weight,
+                                 void* out, void* residual_out, int rows, int hidden, float eps, void* const* buffers,
+                                 int rank, int world, size_t max_message_bytes, void* stream) {
+    return rmsnorm_allreduce_impl(x, x_row_stride, residual, weight, out, residual_out, rows, hidden, eps, buffers, rank,
+                                  world, max_message_bytes, 1, stream);
 }
 
 }  // extern "C"

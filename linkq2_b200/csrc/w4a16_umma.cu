@@ -64,6 +64,7 @@ struct UParams {
     int stages_per_rank;
     int early_weights;    // request weight bytes before the previous kernel of the stream has finished
     int silu;             // columns are interleaved [4 gate | 4 up]: write silu(gate) * up, N / 2 wide
+    PushTarget push;      // tensor-parallel peers that receive the output as flagged words (world 0: none)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -496,15 +497,33 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                         silu_mul_quad(slice_sum(ml, col), slice_sum(ml, col + 4));
             }
         } else {
+            // Row-split projections under tensor parallelism: besides y, every finished quad goes
+            // straight into the peers' exchange buffers as one flagged 16-byte word {2 halves, seq,
+            // 2 halves, seq} (the format lq2_rmsnorm_allreduce gathers), so the transfer overlaps
+            // the rest of this kernel instead of starting when the consumer does.
+            const int world = p.push.world, me = p.push.rank;
+            unsigned int seq = 0;
+            size_t ll = 0;
+            if (world > 1) {
+                seq = *reinterpret_cast<const unsigned int*>(p.push.peers.base[me]) + 1;   // exchanges completed + 1
+                ll = llslots_offset(world, p.push.max_bytes) +
+                     (size_t(seq & 1u) * world + me) * 2 * p.push.max_bytes;
+            }
             const int quads = W / 4;
             for (int e = tid; e < rows * quads; e += kUThreads) {
                 const int ml = e / quads, col = (e - ml * quads) * 4;
                 const float4 sum = slice_sum(ml, col);
                 const int nn = tile_n0 + rank * W + col;
                 if (nn < p.n) {
-                    const __half2 lo = __floats2half2_rn(sum.x, sum.y);
-                    const __half2 hi = __floats2half2_rn(sum.z, sum.w);
-                    *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * p.n + nn) = make_uint2(h2_as_u32(lo), h2_as_u32(hi));
+                    const uint32_t lo = h2_as_u32(__floats2half2_rn(sum.x, sum.y));
+                    const uint32_t hi = h2_as_u32(__floats2half2_rn(sum.z, sum.w));
+                    *reinterpret_cast<uint2*>(p.y + int64_t(m0 + ml) * p.n + nn) = make_uint2(lo, hi);
+                    if (world > 1) {
+                        const size_t off = ll + (size_t(m0 + ml) * (p.n / 8) + (nn >> 3)) * 32 + ((nn >> 2) & 1) * 16;
+                        const uint4 word = make_uint4(lo, seq, hi, seq);
+                        for (int peer = 0; peer < world; ++peer)
+                            if (peer != me) *reinterpret_cast<uint4*>(p.push.peers.base[peer] + off) = word;
+                    }
                 }
             }
         }
@@ -691,13 +710,19 @@ int launch_umma_z(const __half* x, int64_t ldx, const int32_t* packed, const __h
 }  // namespace
 
 int w4a16_umma_launch(const __half* x, int64_t ldx, const int32_t* packed, const __half* scales,
-                      const __half* zeros, __half* y, int m, int n, int k, int group, int silu, cudaStream_t st) {
+                      const __half* zeros, __half* y, int m, int n, int k, int group, int silu,
+                      const PushTarget* push, cudaStream_t st) {
     const UPlan pl = make_uplan(m, n, k);
     if (pl.m_tiles > 65535) return LQ2_ERR_SHAPE;
     UParams p;
     p.y = y; p.m = m; p.n = n; p.k = k; p.group = group; p.stages_per_rank = pl.spr;
     p.early_weights = early_weight_fetch() ? 1 : 0;
     p.silu = silu;
+    p.push = PushTarget{};
+    if (push) {
+        if (pl.mb > 64 || silu) return LQ2_ERR_SHAPE;      // only the pushed-reduction epilogue carries it
+        p.push = *push;
+    }
     switch (pl.mb) {
         case 16: return launch_umma_z<16>(x, ldx, packed, scales, zeros, p, pl, st);
         case 32: return launch_umma_z<32>(x, ldx, packed, scales, zeros, p, pl, st);

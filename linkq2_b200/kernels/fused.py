@@ -39,11 +39,13 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.T
     return out if residual is None else (out, res_out.view(x.shape))
 
 
-def rmsnorm_allreduce(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor, exchange):
+def rmsnorm_allreduce(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor, exchange,
+                      pushed: bool = False):
     """``rmsnorm(all_reduce(x), weight, eps, residual)`` in one launch: ``x`` is this
     rank's partial sum; the exchange runs over peer memory inside the norm kernel
     (``exchange``: the ``PeerExchange`` of the tensor-parallel group).  Returns
-    ``(normalised, all_reduce(x) + residual)``."""
+    ``(normalised, all_reduce(x) + residual)``.  ``pushed``: the projection that produced
+    ``x`` has already sent it to the peers (``linear(..., push_to=exchange)``); only gather."""
     if x.dtype != torch.float16 or not x.is_cuda:
         raise TypeError("rmsnorm_allreduce runs on CUDA fp16 tensors")
     hidden = x.shape[-1]
@@ -56,7 +58,8 @@ def rmsnorm_allreduce(x: torch.Tensor, weight: torch.Tensor, eps: float, residua
     out = torch.empty((rows, hidden), dtype=torch.float16, device=x.device)
     res_out = torch.empty_like(out)
     with torch.cuda.device(x.device):
-        status = _lib.lib.lq2_rmsnorm_allreduce(
+        entry = _lib.lib.lq2_rmsnorm_allreduce_pushed if pushed else _lib.lib.lq2_rmsnorm_allreduce
+        status = entry(
             x2.data_ptr(), x2.stride(0), res_in.data_ptr(), weight.data_ptr(), out.data_ptr(), res_out.data_ptr(),
             rows, hidden, eps, exchange.table, exchange.rank, exchange.world, exchange.max_bytes, _stream(x))
     _lib.check(status, "lq2_rmsnorm_allreduce")

@@ -16,8 +16,14 @@ def set_constant_weights(enabled: bool) -> bool:
     return bool(_lib.lib.lq2_w4a16_set_constant_weights(1 if enabled else 0))
 
 
+def can_push(rows: int, n: int, exchange) -> bool:
+    """Shapes for which ``linear(..., push_to=exchange)`` exists: the tcgen05 kernel's pushed
+    reduction (8 < rows <= 64) and a message that fits the exchange buffer."""
+    return exchange is not None and 8 < rows <= 64 and rows * n * 2 <= exchange.max_bytes
+
+
 def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
-           meta, *, gate_up_silu: bool = False) -> torch.Tensor:
+           meta, *, gate_up_silu: bool = False, push_to=None) -> torch.Tensor:
     """``x [..., K] fp16`` times the dequantised ``[K, N]`` weight -> ``[..., N] fp16``.
 
     ``packed [K/8, N] int32``, ``scales [K/G, N] fp16``; ``zeros`` is either the
@@ -31,6 +37,11 @@ def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: t
     gate and an up projection with their columns interleaved in blocks of four
     (``B200Linear.fuse_gate_up``); the result is ``silu(gate(x)) * up(x)``, ``N / 2`` wide
     (``lq2_w4a16_gate_up_silu``).
+
+    ``push_to`` (a ``PeerExchange``): the projection is row-split under tensor parallelism;
+    besides returning this rank's partial sum the kernel sends it to the peers' exchange
+    buffers (``lq2_w4a16_linear_push``).  Only for ``can_push(rows, n, exchange)`` shapes;
+    the next exchange call must be ``rmsnorm_allreduce(..., pushed=True)`` on the result.
     """
     if meta[0] != 4 or meta[9] != 3:
         raise ValueError("only 4-bit weights with (u - zero) * scale dequantisation are supported")
@@ -59,6 +70,13 @@ def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, zeros: t
         need = _lib.lib.lq2_w4a16_workspace_bytes(m, n, k)
         ws = _workspace.get("w4a16", need, x.device) if need else None
         stream = torch.cuda.current_stream().cuda_stream
+        if push_to is not None:
+            status = _lib.lib.lq2_w4a16_linear_push(
+                x2.data_ptr(), x2.stride(0), packed.data_ptr(), scales.data_ptr(), zero_ptr, y.data_ptr(),
+                m, n, k, group, push_to.table, push_to.rank, push_to.world, push_to.max_bytes, stream)
+            _lib.check(status, "lq2_w4a16_linear_push")
+            _lib.count()
+            return y.view(shape)
         entry = _lib.lib.lq2_w4a16_gate_up_silu if gate_up_silu else _lib.lib.lq2_w4a16_linear
         status = entry(
             x2.data_ptr(), x2.stride(0), packed.data_ptr(), scales.data_ptr(), zero_ptr, y.data_ptr(),

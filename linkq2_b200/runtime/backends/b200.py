@@ -109,6 +109,13 @@ class B200Linear(QuantLinear):
         _weights_complete(fused.packed.device)
         return fused
 
+    def forward_push(self, x, exchange):
+        """``forward`` of a row-split projection that also sends the partial sum to the
+        tensor-parallel peers (see ``ops.linear``)."""
+        if x.dtype != self.compute_dtype:
+            raise TypeError(f"expected {self.compute_dtype}, got {x.dtype}")
+        return linear(x, self.packed, self.scales, self.zeros, self._meta, push_to=exchange)
+
     def forward(self, x):
         if getattr(self, "gate_up_silu", False):
             if x.dtype != self.compute_dtype:

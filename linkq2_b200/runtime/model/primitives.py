@@ -21,7 +21,7 @@ class RMSNorm(nn.Module):
         from linkq2_b200.kernels.fused import rmsnorm, rmsnorm_allreduce
         if deferred:
             from linkq2_b200.runtime.parallel import get_tp
-            return rmsnorm_allreduce(x, self.weight, self.eps, residual, get_tp().exchange)
+            return rmsnorm_allreduce(x, self.weight, self.eps, residual, get_tp().exchange, pushed=deferred == 2)
         return rmsnorm(x, self.weight, self.eps, residual)
 
     def reference_forward(self, x, residual=None):

@@ -120,7 +120,7 @@ class Qwen3Attention(nn.Module):
                              slot_mapping=ctx.slot_mapping if store else None, v_group=attn.v_group,
                              want_k=ctx.is_prefill)
         o = attn.attend(q, k, v)
-        return self.tp.reduce_or_defer(self.o_proj(o.flatten(1, -1)))
+        return self.tp.project_reduce_or_defer(self.o_proj, o.flatten(1, -1))
 
 
 class Qwen3MLP(nn.Module):
@@ -148,7 +148,7 @@ class Qwen3MLP(nn.Module):
             hidden = silu_mul(*self.gate_up_proj(x).chunk(2, dim=-1))
         else:
             hidden = silu_mul(self.gate_proj(x), self.up_proj(x))
-        return self.tp.reduce_or_defer(self.down_proj(hidden))
+        return self.tp.project_reduce_or_defer(self.down_proj, hidden)
 
 
 class Qwen3DecoderLayer(nn.Module):

@@ -99,6 +99,7 @@ class TensorParallel:
     size: int = 1
     group: object | None = None
     exchange: PeerExchange | None = None
+    push_enabled: bool = True        # LQ2_PEER_PUSH=0: the norm kernel sends the partial sums itself
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         """Sum over the ranks, in place.  Small fp16 activations go through the
@@ -117,6 +118,19 @@ class TensorParallel:
         if self.size > 1 and self.exchange is not None and self.exchange.accepts(x):
             return x, True
         return self.all_reduce(x), False
+
+    def project_reduce_or_defer(self, layer, x: torch.Tensor):
+        """``reduce_or_defer(layer(x))`` for a row-split projection, with one more outcome:
+        ``deferred == 2`` when the projection kernel itself has pushed its partial sum to the
+        peers, so that the following norm only gathers.  Shape-only decision."""
+        if self.size > 1 and self.exchange is not None and self.push_enabled:
+            from linkq2_b200.kernels.gemlite.ops import can_push
+            rows = x.numel() // x.shape[-1]
+            if (hasattr(layer, "forward_push") and getattr(layer, "input_scale", None) is None
+                    and not getattr(layer, "gate_up_silu", False) and can_push(rows, layer.out_features, self.exchange)):
+                return layer.forward_push(x, self.exchange), 2
+        y, deferred = self.reduce_or_defer(layer(x))
+        return y, int(deferred)
 
     def check_geometry(self, hidden, intermediate, num_heads, num_kv_heads, group_size):
         t = self.size
@@ -162,6 +176,7 @@ def init_from_env(backend: str | None = None, peer_exchange_bytes: int = 4 << 20
             and os.environ.get("LQ2_PEER_ALLREDUCE", "1") != "0"):
         device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         tp.exchange = PeerExchange.create(tp.rank, tp.size, device, peer_exchange_bytes)
+        tp.push_enabled = os.environ.get("LQ2_PEER_PUSH", "1") != "0"
     set_tp(tp)
     return get_tp()
 

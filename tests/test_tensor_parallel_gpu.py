@@ -86,6 +86,25 @@ def _exchange_worker(rank, world, port, results):
             torch.cuda.synchronize()
             assert torch.equal(got_res, want_res) and torch.equal(got_out, want_out), (rows, hidden)
             checked += 1
+    # the producer side fused into the projection: the kernel pushes, the norm only gathers
+    from linkq2_b200.runtime.backends import make_quant_linear
+    for rows, k, n in [(32, 512, 4096), (16, 1536, 4096), (64, 256, 1024), (9, 512, 4096)]:
+        gw = torch.Generator().manual_seed(1000 * rank + k)
+        vals = (torch.randint(0, 16, (n, k), generator=gw, dtype=torch.uint8).to(torch.int16) - 8).to(torch.int8)
+        scale = (torch.rand(n, k // 128, generator=gw) * 0.01 + 0.001).half()
+        layer = make_quant_linear("b200", vals, scale, group_size=128, symmetric=True, device="cuda",
+                                  dtype=torch.float16)
+        xin = torch.randn(rows, k, generator=g).half().cuda()
+        res = torch.randn(rows, n, generator=torch.Generator().manual_seed(rows + n)).half().cuda()
+        w = (1 + 0.1 * torch.randn(n, generator=torch.Generator().manual_seed(n))).half().cuda()
+        for _ in range(2):
+            want_out, want_res = rmsnorm_allreduce(layer(xin), w, 1e-6, res, tp.exchange)
+            partial = layer.forward_push(xin, tp.exchange)
+            got_out, got_res = rmsnorm_allreduce(partial, w, 1e-6, res, tp.exchange, pushed=True)
+            torch.cuda.synchronize()
+            assert torch.equal(partial, layer(xin))
+            assert torch.equal(got_res, want_res) and torch.equal(got_out, want_out), (rows, k, n)
+        checked += 1
     big = torch.ones(2048, 4096, dtype=torch.float16, device="cuda")           # above the limit: NCCL
     assert not tp.exchange.accepts(big)
     assert torch.equal(tp.all_reduce(big), torch.full_like(big, world))
@@ -124,7 +143,7 @@ def test_peer_memory_all_reduce_is_bit_exact():
         results = dict(results)
     if any(v == "unavailable" for v in results.values()):
         pytest.skip("CUDA IPC / peer access is not available between these GPUs")
-    assert results == {0: 28, 1: 28}
+    assert results == {0: 32, 1: 32}
 
 
 @pytest.mark.parametrize("eager", [True, False])

@@ -77,6 +77,15 @@ constexpr int kMaxCtas = 256;
 struct PeerTable {
     unsigned char* base[kMaxWorld];
 };
+// peers.base[i] for a run-time i without indexing the by-value table dynamically (which
+// would make the compiler copy it to local memory at kernel entry)
+__device__ __forceinline__ unsigned char* peer_base(const PeerTable peers, int i) {
+    unsigned char* p = nullptr;
+#pragma unroll
+    for (int k = 0; k < kMaxWorld; ++k)
+        if (k == i) p = peers.base[k];
+    return p;
+}
 // Where a projection kernel pushes its output for the all-reduce that follows it; world == 0: nowhere.
 struct PushTarget {
     PeerTable peers;

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const __half* 
     pdl_wait();
     __shared__ unsigned int s_seq;
     const int b = blockIdx.x, tid = threadIdx.x;
-    unsigned char* mine = peers.base[rank];
+    unsigned char* mine = peer_base(peers, rank);
     unsigned int* calls = reinterpret_cast<unsigned int*>(mine);
     unsigned int* done = calls + 1;
     if (tid == 0) s_seq = *calls + 1;
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const __half* 
         const uint4 v = x4[u];
         for (int p = 0; p < world; ++p) {
             if (p == rank) continue;
-            uint4* dst = reinterpret_cast<uint4*>(peers.base[p] + slots + (size_t(q) * world + rank) * max_bytes);
+            uint4* dst = reinterpret_cast<uint4*>(peer_base(peers, p) + slots + (size_t(q) * world + rank) * max_bytes);
             dst[u] = v;
         }
     }
@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const __half* 
     __syncthreads();
     // (2) tell every peer, (3) wait for every peer
     if (tid < world && tid != rank) {
-        unsigned int* theirs = reinterpret_cast<unsigned int*>(peers.base[tid] + flags_offset()) +
+        unsigned int* theirs = reinterpret_cast<unsigned int*>(peer_base(peers, tid) + flags_offset()) +
                                (size_t(q) * world + rank) * kMaxCtas + b;
         st_release_sys(theirs, seq);
         const unsigned int* own = reinterpret_cast<const unsigned int*>(mine + flags_offset()) +
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
     __shared__ float partial[kNormThreads / 32];
     __shared__ unsigned int s_seq;
     const int row = blockIdx.x, tid = threadIdx.x;
-    unsigned char* mine = peers.base[rank];
+    unsigned char* mine = peer_base(peers, rank);
     unsigned int* calls = reinterpret_cast<unsigned int*>(mine);
     unsigned int* done = calls + 1;
     if (tid == 0) s_seq = *calls + 1;
@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
             const size_t off = ll + size_t(rank) * 2 * max_bytes + (size_t(row) * chunks + idx) * 32;
             for (int p = 0; p < world; ++p) {
                 if (p == rank || pushed) continue;          // pushed: the producing kernel has sent it already
-                uint4* dst = reinterpret_cast<uint4*>(peers.base[p] + off);
+                uint4* dst = reinterpret_cast<uint4*>(peer_base(peers, p) + off);
                 dst[0] = lo;
                 dst[1] = hi;
             }

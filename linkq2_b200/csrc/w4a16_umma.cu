@@ -505,7 +505,11 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             unsigned int seq = 0;
             size_t ll = 0;
             if (world > 1) {
-                seq = *reinterpret_cast<const unsigned int*>(p.push.peers.base[me]) + 1;   // exchanges completed + 1
+                const unsigned char* mine = nullptr;
+#pragma unroll
+                for (int peer = 0; peer < kMaxWorld; ++peer)
+                    if (peer == me) mine = p.push.peers.base[peer];
+                seq = *reinterpret_cast<const unsigned int*>(mine) + 1;                  // exchanges completed + 1
                 ll = llslots_offset(world, p.push.max_bytes) +
                      (size_t(seq & 1u) * world + me) * 2 * p.push.max_bytes;
             }
@@ -521,8 +525,9 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                     if (world > 1) {
                         const size_t off = ll + (size_t(m0 + ml) * (p.n / 8) + (nn >> 3)) * 32 + ((nn >> 2) & 1) * 16;
                         const uint4 word = make_uint4(lo, seq, hi, seq);
-                        for (int peer = 0; peer < world; ++peer)
-                            if (peer != me) *reinterpret_cast<uint4*>(p.push.peers.base[peer] + off) = word;
+#pragma unroll
+                        for (int peer = 0; peer < kMaxWorld; ++peer)   // constant indices: the table stays in parameter space
+                            if (peer < world && peer != me) *reinterpret_cast<uint4*>(p.push.peers.base[peer] + off) = word;
                     }
                 }
             }

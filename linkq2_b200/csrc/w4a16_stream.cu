@@ -574,20 +574,17 @@ size_t w4a16_stream_workspace_bytes(int, int, int) { return 0; }
 int w4a16_stream_launch(const __half* x, int64_t ldx, const int32_t* packed, const __half* scales,
                         const __half* zeros, __half* y, int m, int n, int k, int group, int silu,
                         void*, size_t, cudaStream_t st) {
+    if (m > 8) return LQ2_ERR_SHAPE;
     const Plan pl = make_plan(m, n, k);
-    if (pl.m_tiles > 65535) return LQ2_ERR_SHAPE;
     W4Params p;
     p.x = x; p.ldx = ldx; p.packed = packed; p.scales = scales; p.zeros = zeros; p.y = y;
     p.m = m; p.n = n; p.k = k; p.group = group;
     p.stages_per_rank = pl.spr;
     p.early_weights = early_weight_fetch() ? 1 : 0;
     p.silu = silu;
-    switch (pl.nj) {
-        case 1: return launch_z<1>(p, pl, st);
-        case 2: return launch_z<2>(p, pl, st);
-        case 4: return launch_z<4>(p, pl, st);
-        default: return launch_z<8>(p, pl, st);
-    }
+    // Only the 8-row variant is built: larger batches go to the tcgen05 kernel, which is faster
+    // from 9 rows on (the kernel template itself is generic in the number of 8-row blocks).
+    return launch_z<1>(p, pl, st);
 }
 
 }  // namespace lq2

@@ -14,6 +14,14 @@ and the KV4 cache arithmetic of :mod:`oracle.kv4`:
 
 Activations are held in fp16 between operators and every operator computes in
 fp32, which is where the GPU runtime rounds as well.
+
+Pinned: ``tests/golden/qwen3_tiny.npz`` holds logits and greedy tokens of the
+reference's CPU whole-model path (HF ``Qwen3ForCausalLM`` built by
+``adapters/model_builder.py:19-30`` with ``fake=True`` weights from a checkpoint
+written by the reference's own pipeline); ``kv_mode='fp16'`` runs this restatement
+with the cache quantization bypassed, as that model has none, and
+``tests/test_oracle_golden.py`` compares the two.  The KV4 arithmetic itself is
+pinned by the kernel-level fixtures of :mod:`oracle.kv4`.
 """
 from __future__ import annotations
 
@@ -41,9 +49,14 @@ class OracleQwen3:
     (dequantised), norms/embedding fp16.  ``kscale``/``lam``: ``[L, HKV, D]``."""
 
     def __init__(self, cfg, weights: dict, kscale: torch.Tensor, lam: torch.Tensor | None = None,
-                 v_group: int = 64, max_tokens: int = 4096):
+                 v_group: int = 64, max_tokens: int = 4096, kv_mode: str = "kv4"):
+        if kv_mode not in ("kv4", "fp16"):
+            raise ValueError("kv_mode is 'kv4' or 'fp16'")
         self.cfg, self.w, self.v_group = cfg, weights, v_group
         self.lam = lam
+        self.kv_mode = kv_mode
+        self.history = [[torch.zeros(0, cfg.num_key_value_heads, cfg.head_dim, dtype=torch.float16)] * 2
+                        for _ in range(cfg.num_hidden_layers)]    # fp16 K, V per layer (kv_mode 'fp16')
         self.pools = []
         for layer in range(cfg.num_hidden_layers):
             kc, vc = kv4.empty_pool(max_tokens, cfg.num_key_value_heads, cfg.head_dim, v_group)
@@ -83,9 +96,16 @@ class OracleQwen3:
                 q = q * lam.repeat_interleave(rep, 0)
                 k = k / lam
             kc, vc = self.pools[li]
-            kv4.store_kv_quant(k, v, kc, vc, pos.to(torch.int32), v_group=self.v_group)
             end = self.length + t
-            if mode == "prefill":
+            if self.kv_mode == "fp16":
+                kh, vh = self.history[li]
+                self.history[li] = [torch.cat([kh, k]), torch.cat([vh, v])]
+                kk, vv = self.history[li][0].float(), self.history[li][1].float()
+            else:
+                kv4.store_kv_quant(k, v, kc, vc, pos.to(torch.int32), v_group=self.v_group)
+            if self.kv_mode == "fp16":
+                pass                                  # no cache quantization: every row sees fp16 K/V
+            elif mode == "prefill":
                 kp, vp = kv4.materialize_kv(kc, vc, torch.arange(self.length), v_group=self.v_group)
                 kk = torch.cat([kp, k]).float()
                 vv = torch.cat([vp, v]).float()

@@ -42,6 +42,11 @@ def rebind(serve_gemlite: bool = False) -> None:
         attention.paged_attention_decode = ours.paged_attention_decode
         attention.materialize_kv = ours.materialize_kv
 
+    # a backend committed inside qslab would derive from qslab's QuantLinear; from outside,
+    # B200Linear joins that ABC as a registered subclass (same three methods, same buffers)
+    from qslab.runtime.backends.base import QuantLinear as RefQuantLinear
+    RefQuantLinear.register(B200Linear)
+
     stock = ref_backends.make_quant_linear
     ref_backends.QUANT_BACKENDS = ("gemlite", "b200")
 

@@ -197,7 +197,7 @@ def section_tokens(args):
                 rec["build_s"] = round(time.time() - t0, 1)
                 g = torch.Generator().manual_seed(11)
                 prompt = torch.randint(0, kw["vocab_size"] - 1, (prompt_len,), generator=g).tolist()
-                max_len = (prompt_len + new_tokens + 255) // 256 * 256
+                max_len = (prompt_len + new_tokens + 8 + 255) // 256 * 256
                 ours, ours_ms, ours_first, ours_last = ours_generate(quantized, 0.5, kw, prompt, new_tokens, max_len)
                 rec.update(ours_tokens=ours[:64], ours_tpot_ms=round(ours_ms, 3), distinct_tokens=len(set(ours)))
                 try:

@@ -3,10 +3,18 @@
  *
  * Every entry point takes raw device pointers, sizes, element strides and a
  * CUDA stream (a cudaStream_t passed as void*), enqueues its kernels on that
- * stream and returns at once.  Nothing here allocates, frees or synchronises;
- * no entry point keeps state between calls.  The return value is LQ2_OK or an
- * LQ2_ERR_* code describing which argument was rejected; a rejected call
- * launches nothing.
+ * stream and returns at once.  The return value is LQ2_OK or an LQ2_ERR_* code
+ * describing which argument was rejected; a rejected call launches nothing.
+ *
+ * The compute entry points allocate nothing, free nothing, never synchronise
+ * and keep no state between calls.  The exceptions, each marked below:
+ *   - two process-wide switches, lq2_w4a16_set_constant_weights and
+ *     lq2_allreduce_set_poll_limit (a launch uses the value at launch time);
+ *   - the tensor-parallel setup calls lq2_allreduce_buffer_create/open/close,
+ *     which allocate, map and free device memory and synchronise;
+ *   - lq2_allreduce_timeouts, which synchronises to read a device counter;
+ *   - lq2_kv4_attention_static, whose scratch is one array inside the library
+ *     that keeps the previous call's contents.
  *
  * Paths cited below are relative to the LinkQ2 project root and name the
  * reference interface each function stands in for.
@@ -133,6 +141,16 @@ int lq2_w4a16_gate_up_silu(const void* x, int64_t x_row_stride, const int32_t* p
 int lq2_kv4_store(const void* k, const void* v, int64_t k_stride, int64_t v_stride,
                   uint32_t* kq, const void* ks, uint32_t* vq, void* vs, const int32_t* slots,
                   int tokens, int hkv, int d, int v_group, int64_t num_slots, void* stream);
+
+/*
+ * The same for fp32 keys and values: the reference's kernel converts whatever element
+ * type it is given to fp32 before it quantizes (store.py:31,45), and its own tests store
+ * fp32 tensors (tests/kernels/test_kv4_verify.py:98-102), so fp32 inputs are quantized
+ * from their full precision, not rounded to fp16 first.  Strides in fp32 elements.
+ */
+int lq2_kv4_store_f32(const float* k, const float* v, int64_t k_stride, int64_t v_stride,
+                      uint32_t* kq, const void* ks, uint32_t* vq, void* vs, const int32_t* slots,
+                      int tokens, int hkv, int d, int v_group, int64_t num_slots, void* stream);
 
 /*
  * Number of KV splits lq2_kv4_attention will use.  It depends on shapes only
@@ -349,6 +367,16 @@ int lq2_rmsnorm_allreduce_pushed(const void* x, int64_t x_row_stride, const void
 /* Number of abandoned waits on the current device since the library was loaded
  * (synchronises the device); 0 in a healthy run. */
 unsigned int lq2_allreduce_timeouts(void);
+
+/*
+ * How long a thread of the exchange kernels waits for its peers: `polls` looks at the
+ * exchange buffer in total per thread and launch, over all the pieces it waits for
+ * (<= 0 restores the default, 2^22, a few seconds).  Process-wide; a launch (or a
+ * captured graph node) keeps the value it was issued with.  Returns the previous value.
+ * A thread that runs out stops waiting, the kernel completes with an invalid result and
+ * lq2_allreduce_timeouts() counts it: a peer that has left costs seconds, not a hang.
+ */
+long long lq2_allreduce_set_poll_limit(long long polls);
 
 #ifdef __cplusplus
 }

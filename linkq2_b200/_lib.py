@@ -33,6 +33,7 @@ SIGNATURES = {
     "lq2_w4a16_linear_push": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                       c_int, c_void_p, c_int, c_int, c_size_t, c_void_p]),
     "lq2_allreduce_timeouts": (c_uint, []),
+    "lq2_allreduce_set_poll_limit": (ctypes.c_longlong, [ctypes.c_longlong]),
     "lq2_w4a16_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "lq2_w4a16_linear": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
@@ -40,6 +41,8 @@ SIGNATURES = {
                                        c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "lq2_kv4_store": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p]),
+    "lq2_kv4_store_f32": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p]),
     "lq2_kv4_attention_splits": (c_int, [c_int] * 7),
     "lq2_kv4_attention_workspace_bytes": (c_size_t, [c_int] * 7),
     "lq2_kv4_attention": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -11,6 +11,8 @@ int w4a16_umma_launch(const __half*, int64_t, const int32_t*, const __half*, con
                       int, int, int, const PushTarget*, cudaStream_t);
 int kv4_store_launch(const __half*, const __half*, int64_t, int64_t, uint32_t*, const __half*, uint32_t*,
                      __half*, const int32_t*, int, int, int, int, int64_t, cudaStream_t);
+int kv4_store_f32_launch(const float*, const float*, int64_t, int64_t, uint32_t*, const __half*, uint32_t*,
+                         __half*, const int32_t*, int, int, int, int, int64_t, cudaStream_t);
 int kv4_materialize_launch(const uint32_t*, const __half*, const uint32_t*, const __half*, const int64_t*,
                            __half*, __half*, int, int, int, int, int64_t, cudaStream_t);
 int kv4_attention_splits(int, int, int, int, int, int, int);
@@ -153,6 +155,19 @@ int lq2_kv4_store(const void* k, const void* v, int64_t k_stride, int64_t v_stri
     return kv4_store_launch(static_cast<const __half*>(k), static_cast<const __half*>(v), k_stride,
                             v_stride, kq, static_cast<const __half*>(ks), vq, static_cast<__half*>(vs),
                             slots, tokens, hkv, d, v_group, num_slots, static_cast<cudaStream_t>(stream));
+}
+
+int lq2_kv4_store_f32(const float* k, const float* v, int64_t k_stride, int64_t v_stride, uint32_t* kq,
+                      const void* ks, uint32_t* vq, void* vs, const int32_t* slots, int tokens, int hkv,
+                      int d, int v_group, int64_t num_slots, void* stream) {
+    if (tokens == 0) return LQ2_OK;
+    if (!k || !v || !kq || !ks || !vq || !vs || !slots || tokens < 0 || hkv <= 0 || d <= 0 || num_slots <= 0)
+        return LQ2_ERR_ARG;
+    if (d % 8 || v_group < 8 || v_group > 256 || !pow2(v_group) || d % v_group) return LQ2_ERR_SHAPE;
+    if (!aligned(ks, 16) || !aligned(k, 4) || !aligned(v, 4)) return LQ2_ERR_ALIGN;
+    return kv4_store_f32_launch(k, v, k_stride, v_stride, kq, static_cast<const __half*>(ks), vq,
+                                static_cast<__half*>(vs), slots, tokens, hkv, d, v_group, num_slots,
+                                static_cast<cudaStream_t>(stream));
 }
 
 int lq2_kv4_attention_splits(int batch, int verify_m, int hq, int hkv, int d, int page, int max_blocks) {

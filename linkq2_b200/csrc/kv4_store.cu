@@ -36,15 +36,28 @@ __device__ __forceinline__ void load8(const __half* p, float (&f)[8]) {
         for (int i = 0; i < 8; ++i) f[i] = __half2float(p[i]);
     }
 }
+// fp32 keys / values: the reference's kernel converts whatever it loads to fp32
+// (store.py:31,45), so fp32 inputs are quantized from their full precision
+template <bool VEC>
+__device__ __forceinline__ void load8(const float* p, float (&f)[8]) {
+    if (VEC) {
+        const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = p[i];
+    }
+}
 
 __device__ __forceinline__ uint32_t encode(float x, float s) {
     const float q = floorf(fminf(fmaxf(__fdiv_rn(x, s), -8.0f), 7.0f) + 0.5f);
     return uint32_t(int(q) + 8) & 15u;
 }
 
-template <bool VEC>
+template <bool VEC, typename T>
 __global__ void __launch_bounds__(256) kv4_store_kernel(
-    const __half* __restrict__ k, const __half* __restrict__ v, int64_t k_stride, int64_t v_stride,
+    const T* __restrict__ k, const T* __restrict__ v, int64_t k_stride, int64_t v_stride,
     uint32_t* __restrict__ kq, const __half* __restrict__ ks, uint32_t* __restrict__ vq,
     __half* __restrict__ vs, const int32_t* __restrict__ slots, int tokens, int hkv, int nw,
     int words_per_group, int64_t num_slots) {
@@ -133,18 +146,32 @@ __global__ void __launch_bounds__(256) kv4_materialize_kernel(
 
 }  // namespace
 
-int kv4_store_launch(const __half* k, const __half* v, int64_t k_stride, int64_t v_stride, uint32_t* kq,
-                     const __half* ks, uint32_t* vq, __half* vs, const int32_t* slots, int tokens,
-                     int hkv, int d, int v_group, int64_t num_slots, cudaStream_t st) {
+template <typename T>
+static int store_launch(const T* k, const T* v, int64_t k_stride, int64_t v_stride, uint32_t* kq,
+                        const __half* ks, uint32_t* vq, __half* vs, const int32_t* slots, int tokens,
+                        int hkv, int d, int v_group, int64_t num_slots, cudaStream_t st) {
     const int nw = d / 8, wpg = v_group / 8;
     const int64_t total = int64_t(tokens) * hkv * nw;
     const int blocks = int(cdiv64(total, 256));
-    const bool vec = aligned(k, 16) && aligned(v, 16) && k_stride % 8 == 0 && v_stride % 8 == 0;
+    constexpr int kVecElems = 16 / int(sizeof(T));       // elements per 16-byte access
+    const bool vec = aligned(k, 16) && aligned(v, 16) && k_stride % kVecElems == 0 && v_stride % kVecElems == 0;
     if (vec)
-        return launch_pdl(kv4_store_kernel<true>, dim3(blocks), dim3(256), 0, st, 1, k, v, k_stride, v_stride, kq, ks,
-                          vq, vs, slots, tokens, hkv, nw, wpg, num_slots);
-    return launch_pdl(kv4_store_kernel<false>, dim3(blocks), dim3(256), 0, st, 1, k, v, k_stride, v_stride, kq, ks,
+        return launch_pdl(kv4_store_kernel<true, T>, dim3(blocks), dim3(256), 0, st, 1, k, v, k_stride, v_stride, kq,
+                          ks, vq, vs, slots, tokens, hkv, nw, wpg, num_slots);
+    return launch_pdl(kv4_store_kernel<false, T>, dim3(blocks), dim3(256), 0, st, 1, k, v, k_stride, v_stride, kq, ks,
                       vq, vs, slots, tokens, hkv, nw, wpg, num_slots);
+}
+
+int kv4_store_launch(const __half* k, const __half* v, int64_t k_stride, int64_t v_stride, uint32_t* kq,
+                     const __half* ks, uint32_t* vq, __half* vs, const int32_t* slots, int tokens,
+                     int hkv, int d, int v_group, int64_t num_slots, cudaStream_t st) {
+    return store_launch(k, v, k_stride, v_stride, kq, ks, vq, vs, slots, tokens, hkv, d, v_group, num_slots, st);
+}
+
+int kv4_store_f32_launch(const float* k, const float* v, int64_t k_stride, int64_t v_stride, uint32_t* kq,
+                         const __half* ks, uint32_t* vq, __half* vs, const int32_t* slots, int tokens,
+                         int hkv, int d, int v_group, int64_t num_slots, cudaStream_t st) {
+    return store_launch(k, v, k_stride, v_stride, kq, ks, vq, vs, slots, tokens, hkv, d, v_group, num_slots, st);
 }
 
 int kv4_materialize_launch(const uint32_t* kq, const __half* ks, const uint32_t* vq, const __half* vs,

@@ -33,9 +33,12 @@
 // call's sequence number, so the receiver needs no separate flag and the sender no fence - it
 // polls the chunk itself until all four numbers match, one NVLink crossing in total.
 //
-// Every wait is bounded: after kMaxPolls polls the CTA gives up, counts the failure in
-// g_lq2_allreduce_timeouts and finishes with whatever it has, so a missing peer cannot hang
-// the GPU.  The host reads the counter with lq2_allreduce_timeouts().
+// Every wait is bounded.  A thread has one budget of polls for the whole kernel (the limit set
+// with lq2_allreduce_set_poll_limit, a kernel argument), shared by all the chunks and peers it
+// waits for: once it is spent the thread stops waiting, the failure is counted in
+// g_lq2_allreduce_timeouts and the kernel finishes with whatever it has, so a missing peer
+// costs one budget, not one per wait, and cannot hang the GPU.  The host reads the counter
+// with lq2_allreduce_timeouts().
 #include <cstring>
 
 #include "common.cuh"
@@ -46,7 +49,7 @@ namespace {
 
 constexpr int kArThreads = 512;
 constexpr int kBytesPerCta = kArThreads * 16;          // one 128-bit access per thread and pass
-constexpr long long kMaxPolls = 1ll << 25;              // on the order of ten seconds of polling
+constexpr long long kDefaultPollLimit = 1ll << 22;      // a few seconds of polling per thread
 
 __device__ unsigned int g_lq2_allreduce_timeouts = 0;
 
@@ -78,7 +81,7 @@ __device__ __forceinline__ void add8(float (&acc)[8], const uint4& v) {
 __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const __half* x, __half* out,
                                                                   const PeerTable peers, const int rank,
                                                                   const int world, const size_t bytes,
-                                                                  const size_t max_bytes) {
+                                                                  const size_t max_bytes, const long long poll_limit) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ unsigned int s_seq;
@@ -117,7 +120,7 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const __half* 
                                   (size_t(q) * world + tid) * kMaxCtas + b;
         long long polls = 0;
         while (ld_acquire_sys(own) != seq) {
-            if (++polls >= kMaxPolls) {
+            if (++polls >= poll_limit) {
                 atomicAdd(&g_lq2_allreduce_timeouts, 1u);
                 break;
             }
@@ -170,7 +173,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
     const __half* x, int64_t x_stride, const __half* residual, const __half* __restrict__ weight, __half* out,
     __half* residual_out, const int hidden, const float eps, const PeerTable peers, const int rank,
-    const int world, const size_t max_bytes, const int pushed) {
+    const int world, const size_t max_bytes, const int pushed, const long long poll_limit) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ float partial[kNormThreads / 32];
@@ -206,6 +209,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
     float v[kNormMaxChunks][8];
     float ss = 0.f;
     bool gave_up = false;
+    long long budget = poll_limit;                      // polls left to this thread, over all its waits
 #pragma unroll
     for (int c = 0; c < kNormMaxChunks; ++c) {
         const int idx = tid + c * kNormThreads;
@@ -218,12 +222,11 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
                 }
                 const unsigned char* src = mine + ll + size_t(p) * 2 * max_bytes + (size_t(row) * chunks + idx) * 32;
                 uint4 lo, hi;
-                long long polls = 0;
                 for (;;) {
                     lo = ld_volatile_u4(src);
                     hi = ld_volatile_u4(src + 16);
                     if (lo.y == seq && lo.w == seq && hi.y == seq && hi.w == seq) break;
-                    if (++polls >= kMaxPolls) {
+                    if (--budget <= 0) {                // spent: this and every later wait ends after one look
                         gave_up = true;
                         break;
                     }
@@ -281,7 +284,17 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
 
 using namespace lq2;
 
+#include <atomic>
+
+namespace {
+std::atomic<long long> g_poll_limit{kDefaultPollLimit};
+}  // namespace
+
 extern "C" {
+
+long long lq2_allreduce_set_poll_limit(long long polls) {
+    return g_poll_limit.exchange(polls > 0 ? polls : kDefaultPollLimit, std::memory_order_relaxed);
+}
 
 size_t lq2_allreduce_buffer_bytes(int world, size_t max_message_bytes) {
     if (world < 2 || world > kMaxWorld || max_message_bytes == 0 || max_message_bytes % 16) return 0;
@@ -353,7 +366,7 @@ int lq2_allreduce_fp16(const void* x, void* out, int64_t count, void* const* buf
     if (grid > kMaxCtas) grid = kMaxCtas;
     return launch_pdl(tp_allreduce_kernel, dim3(grid), dim3(kArThreads), 0, static_cast<cudaStream_t>(stream), 1,
                       static_cast<const __half*>(x), static_cast<__half*>(out), peers, rank, world, bytes,
-                      max_message_bytes);
+                      max_message_bytes, g_poll_limit.load(std::memory_order_relaxed));
 }
 
 static int rmsnorm_allreduce_impl(const void* x, int64_t x_row_stride, const void* residual, const void* weight,
@@ -375,7 +388,8 @@ static int rmsnorm_allreduce_impl(const void* x, int64_t x_row_stride, const voi
     return launch_pdl(rmsnorm_allreduce_kernel, dim3(rows), dim3(kNormThreads), 0, static_cast<cudaStream_t>(stream), 1,
                       static_cast<const __half*>(x), x_row_stride, static_cast<const __half*>(residual),
                       static_cast<const __half*>(weight), static_cast<__half*>(out),
-                      static_cast<__half*>(residual_out), hidden, eps, peers, rank, world, max_message_bytes, pushed);
+                      static_cast<__half*>(residual_out), hidden, eps, peers, rank, world, max_message_bytes, pushed,
+                      g_poll_limit.load(std::memory_order_relaxed));
 }
 
 int lq2_rmsnorm_allreduce(const void* x, int64_t x_row_stride, const void* residual, const void* weight, void* out,

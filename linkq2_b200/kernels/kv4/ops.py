@@ -19,14 +19,23 @@ def _static_scale(ks: torch.Tensor, hkv: int, d: int) -> None:
 
 def store_kv_quant(k: torch.Tensor, v: torch.Tensor, k_cache, v_cache,
                    slot_mapping: torch.Tensor, v_group: int = 64) -> None:
-    """Quantize ``k, v [T, HKV, D] fp16`` into the pool at ``slot_mapping [T]``
+    """Quantize ``k, v [T, HKV, D]`` into the pool at ``slot_mapping [T]``
     (``-1`` skips).  Same contract as ``qslab/kernels/kv4/store.py:58-68``; token
-    strides are free (slices of a fused QKV buffer), head stride must be ``D``."""
+    strides are free (slices of a fused QKV buffer), head stride must be ``D``.
+    fp16 is the runtime's type; like the reference's kernel, which converts what it
+    loads to fp32 (``store.py:31,45``), fp32 tensors are quantized from their full
+    precision and bf16 ones are widened to fp32 first."""
     t, h, d = k.shape
     kq, ks = k_cache
     vq, vs = v_cache
-    if k.dtype != torch.float16 or v.dtype != torch.float16:
-        raise TypeError("KV4 store takes fp16 keys and values")
+    floats = (torch.float16, torch.float32, torch.bfloat16)
+    if k.dtype not in floats or v.dtype not in floats:
+        raise TypeError("KV4 store takes floating-point keys and values")
+    if not k.is_cuda:
+        raise RuntimeError("linkq2_b200 operators run on CUDA tensors only")
+    wide = k.dtype != torch.float16 or v.dtype != torch.float16
+    if wide:
+        k, v = k.float(), v.float()
     _static_scale(ks, h, d)
     if t == 0:
         return
@@ -39,7 +48,8 @@ def store_kv_quant(k: torch.Tensor, v: torch.Tensor, k_cache, v_cache,
         slots = slots.contiguous()
     with torch.cuda.device(k.device):
         stream = torch.cuda.current_stream().cuda_stream
-        status = _lib.lib.lq2_kv4_store(
+        entry = _lib.lib.lq2_kv4_store_f32 if wide else _lib.lib.lq2_kv4_store
+        status = entry(
             k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), kq.data_ptr(), ks.data_ptr(),
             vq.data_ptr(), vs.data_ptr(), slots.data_ptr(), t, h, d, v_group, kq.shape[0], stream)
     _lib.check(status, "lq2_kv4_store")

@@ -59,6 +59,12 @@ class ModelRunner:
                 verify_rows=config.spec_num_drafts + 1, device=self.device)
             self.cuda_graphs.capture(self._forward)
 
+    def check_exchange(self):
+        """Raise if a wait of the tensor-parallel exchange kernels has run out since the library
+        was loaded (their results were invalid then).  Synchronises the device."""
+        if self.tp.exchange is not None:
+            self.tp.exchange.check()
+
     def shutdown(self):
         """Release the CUDA graphs (call on every rank before the process group is
         destroyed; harmless otherwise)."""
@@ -186,6 +192,7 @@ class ModelRunner:
     def run(self, seqs: list[Sequence], is_prefill: bool, counts: list[int] | None = None) -> list[int]:
         """One step; returns one greedy token per sequence (for prefill: the token
         after the last scheduled position)."""
+        self.tp.guard()                      # a peer that has left: stop on the host, before any launch
         graphs = self.cuda_graphs
         if not is_prefill and graphs is not None and len(seqs) <= max(graphs.batch_sizes):
             return self._finish(seqs, self._decode_packed(seqs), False, None)
@@ -197,12 +204,23 @@ class ModelRunner:
         hidden = self.run_model(input_ids, positions, is_prefill)
         return self._finish(seqs, hidden, is_prefill, counts)
 
+    def _graph_table_width(self, seqs, extra_tokens: int) -> int:
+        """Block-table columns of a graph step: the widest table, but never more than the
+        graphs were captured with (``max_model_len``); blocks a sequence holds beyond that
+        cannot be addressed by a step inside the limit and are left out."""
+        graphs = self.cuda_graphs
+        longest = max(len(seq) for seq in seqs) + extra_tokens
+        if longest > graphs.blocks * self.block_size:
+            raise ValueError(f"sequence of {longest} tokens exceeds max_model_len "
+                             f"({graphs.blocks * self.block_size} tokens in the captured graphs)")
+        return min(max(len(seq.block_table) for seq in seqs), graphs.blocks)
+
     def _decode_packed(self, seqs: list[Sequence]):
         """Decode step through the graphs with one pinned record, one host-to-device copy
         and one staging kernel instead of five copies and seven staging ops."""
         graphs = self.cuda_graphs
         b = len(seqs)
-        width = max(len(seq.block_table) for seq in seqs)
+        width = self._graph_table_width(seqs, 0)
         if self._pinned is None:
             cap = graphs.max_batch * (4 + graphs.blocks)
             self._pinned = torch.empty(cap, dtype=torch.int32, pin_memory=True)
@@ -215,8 +233,8 @@ class ModelRunner:
         rec[3 * b:4 * b] = [len(seq) for seq in seqs]
         tables = rec[4 * b:4 * b + b * width].reshape(b, width)
         for i, seq in enumerate(seqs):
-            n = len(seq.block_table)
-            tables[i, :n] = seq.block_table
+            n = min(len(seq.block_table), width)
+            tables[i, :n] = seq.block_table[:n]
             tables[i, n:] = -1
         n = 4 * b + b * width
         self._packed_dev[:n].copy_(self._pinned[:n], non_blocking=True)
@@ -234,6 +252,7 @@ class ModelRunner:
         there is still one host-to-device copy of the step's record and one device-to-host
         copy of its tokens.  Appends the tokens to the sequences and returns them per step.
         The block tables must already cover ``len(seq) + steps`` positions."""
+        self.tp.guard()
         graphs = self.cuda_graphs
         b = len(seqs)
         if graphs is None or b > max(graphs.batch_sizes):
@@ -245,7 +264,7 @@ class ModelRunner:
                 out.append(tokens)
             return out
         import numpy as np
-        width = max(len(seq.block_table) for seq in seqs)
+        width = self._graph_table_width(seqs, steps - 1)
         for seq in seqs:
             if (len(seq) + steps - 1) // self.block_size >= len(seq.block_table):
                 raise ValueError("run_steps needs block tables that cover every new position")
@@ -255,7 +274,8 @@ class ModelRunner:
         base = np.array([len(seq) for seq in seqs], dtype=np.int64)
         tables = np.full((b, width), -1, dtype=np.int32)
         for i, seq in enumerate(seqs):
-            tables[i, :len(seq.block_table)] = seq.block_table
+            n = min(len(seq.block_table), width)
+            tables[i, :n] = seq.block_table[:n]
         bs = self.block_size
         for i in range(steps):
             pos = base - 1 + i
@@ -297,6 +317,7 @@ class ModelRunner:
     @torch.inference_mode()
     def verify(self, seqs: list[Sequence], drafts: list[list[int]]) -> list[list[int]]:
         """One M-row verify forward; returns the greedy token at every row."""
+        self.tp.guard()
         m_rows = self.config.spec_num_drafts + 1
         input_ids, positions = self.prepare_verify(seqs, drafts)
         hidden = self.run_model(input_ids, positions, False, rows=m_rows)

@@ -17,6 +17,15 @@ import torch
 import torch.distributed as dist
 
 
+class PeerLeft(RuntimeError):
+    """A rank of the tensor-parallel group has announced that it is leaving."""
+
+
+def _store():
+    from torch.distributed.distributed_c10d import _get_default_store
+    return _get_default_store()
+
+
 class PeerExchange:
     """The exchange buffers of ``lq2_allreduce_fp16``: this rank's buffer (allocated
     by the library, shared through CUDA IPC) and the mapped buffers of its peers.
@@ -55,14 +64,19 @@ class PeerExchange:
             agreed = [None] * world
             dist.all_gather_object(agreed, bool(ok), group=group)
             if not all(agreed):
+                # unmap everywhere first, free afterwards: an exported buffer must outlive
+                # every mapping of it in the other processes
                 for peer, ptr in enumerate(pointers):
                     if ptr and peer != rank:
                         lib.lq2_allreduce_buffer_close(ptr, 0)
+                dist.barrier(group=group)
                 if own.value:
                     lib.lq2_allreduce_buffer_close(own.value, 1)
                 return None
         table = (ctypes.c_void_p * world)(*pointers)
-        return cls(rank, world, max_bytes, own.value, table, pointers)
+        exchange = cls(rank, world, max_bytes, own.value, table, pointers)
+        exchange.group = group
+        return exchange
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         from linkq2_b200 import _lib
@@ -83,14 +97,34 @@ class PeerExchange:
         from linkq2_b200 import _lib
         return int(_lib.lib.lq2_allreduce_timeouts())
 
+    def set_poll_limit(self, polls: int) -> int:
+        """Polls a thread of the exchange kernels spends waiting for its peers before it gives
+        up (``lq2_allreduce_set_poll_limit``; <= 0: the default).  Returns the previous limit."""
+        from linkq2_b200 import _lib
+        return int(_lib.lib.lq2_allreduce_set_poll_limit(int(polls)))
+
+    def check(self) -> None:
+        """Raise if any wait of an exchange kernel on this device has run out: the outputs of
+        that launch were invalid (synchronises the device)."""
+        n = self.timeouts()
+        if n:
+            raise RuntimeError(f"tensor-parallel exchange: {n} abandoned waits on rank {self.rank}; "
+                               "a peer did not deliver its part and the results are invalid")
+
     def close(self):
+        """Collective.  Two phases with a barrier between them: every rank unmaps its peers'
+        buffers, and only when all have done so does each rank free its own (freeing an
+        exported allocation that another process still has mapped is undefined)."""
         from linkq2_b200 import _lib
         for peer, ptr in enumerate(self._pointers):
             if ptr and peer != self.rank:
                 _lib.lib.lq2_allreduce_buffer_close(ptr, 0)
+        self._pointers = []
+        if dist.is_available() and dist.is_initialized():
+            dist.barrier(group=getattr(self, "group", None))
         if self._own:
             _lib.lib.lq2_allreduce_buffer_close(self._own, 1)
-        self._pointers, self._own = [], None
+        self._own = None
 
 
 @dataclass
@@ -100,6 +134,25 @@ class TensorParallel:
     group: object | None = None
     exchange: PeerExchange | None = None
     push_enabled: bool = True        # LQ2_PEER_PUSH=0: the norm kernel sends the partial sums itself
+
+    def leave(self) -> None:
+        """Announce on the process group's store that this rank stops taking part.  Call it
+        between steps, with none of this rank's kernels or collectives in flight; the others
+        see it in ``guard()`` before their next launch."""
+        if self.size > 1 and dist.is_initialized():
+            _store().set(f"lq2/left/{self.rank}", b"1")
+
+    def guard(self) -> None:
+        """Raise ``PeerLeft`` if a rank has announced its departure.  The runner calls this on
+        the host before it issues a step: an exchange kernel launched without its peer would
+        only end when its poll budget runs out, with invalid results.  One non-blocking store
+        query per peer."""
+        if self.size == 1 or not dist.is_initialized():
+            return
+        store = _store()
+        gone = [r for r in range(self.size) if r != self.rank and store.check([f"lq2/left/{r}"])]
+        if gone:
+            raise PeerLeft(f"rank(s) {gone} left the tensor-parallel group; rank {self.rank} stops before its next step")
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         """Sum over the ranks, in place.  Small fp16 activations go through the
@@ -154,12 +207,15 @@ def set_tp(tp: TensorParallel) -> None:
     _TP = tp
 
 
-def init_from_env(backend: str | None = None, peer_exchange_bytes: int = 4 << 20) -> TensorParallel:
+def init_from_env(backend: str | None = None, peer_exchange_bytes: int = 4 << 20,
+                  timeout_s: float | None = None) -> TensorParallel:
     """Join the process group described by RANK / WORLD_SIZE / MASTER_* and make
     the whole world one tensor-parallel group.  On NCCL, all-reduces of fp16
     activations of up to ``peer_exchange_bytes`` (decode and verify steps) use the
     library's own kernel over peer memory when the GPUs can map each other's
-    memory; ``LQ2_PEER_ALLREDUCE=0`` keeps everything on NCCL."""
+    memory; ``LQ2_PEER_ALLREDUCE=0`` keeps everything on NCCL.  ``timeout_s`` is the process
+    group's collective timeout: a library collective whose peer never joins ends with an error
+    after that long instead of blocking."""
     import os
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world == 1:
@@ -168,6 +224,9 @@ def init_from_env(backend: str | None = None, peer_exchange_bytes: int = 4 << 20
     if not dist.is_initialized():
         backend = backend or ("nccl" if torch.cuda.is_available() else "gloo")
         kwargs = {}
+        if timeout_s is not None:
+            import datetime
+            kwargs["timeout"] = datetime.timedelta(seconds=timeout_s)
         if backend == "nccl":
             kwargs["device_id"] = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         dist.init_process_group(backend=backend, **kwargs)

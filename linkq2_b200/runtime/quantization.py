@@ -208,3 +208,50 @@ def build_random(cfg: ModelConfig, *, seed=0, group_size=128, device="cuda:0", m
             _set_param(model, name, torch.ones(param.shape, dtype=torch.float16, device=dev))
     model.fuse_projections()
     return model.eval()
+
+
+@torch.no_grad()
+def save_random_checkpoint(path, cfg: ModelConfig, *, seed: int = 0, group_size: int = 128) -> Path:
+    """Write a small seeded RTN-W4 checkpoint in the reference's on-disk layout
+    (``qslab/compression/checkpoint.py:33-63``): every tensor is drawn from one CPU
+    generator, so the same ``(cfg, seed)`` gives the same files wherever it runs.  The LM
+    head is a row permutation of the embedding, which makes greedy decoding on random
+    weights walk through many tokens with large margins.  Used by the self-check of
+    ``bench.py`` and by tests; real checkpoints come from the reference's offline pipeline."""
+    from safetensors.torch import save_file
+    path = Path(path)
+    path.mkdir(parents=True, exist_ok=True)
+    g = torch.Generator().manual_seed(seed)
+    hid, inter, d = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    shapes = {"self_attn.q_proj": (hq * d, hid), "self_attn.k_proj": (hkv * d, hid),
+              "self_attn.v_proj": (hkv * d, hid), "self_attn.o_proj": (hid, hq * d),
+              "mlp.gate_proj": (inter, hid), "mlp.up_proj": (inter, hid), "mlp.down_proj": (hid, inter)}
+    tensors, layers = {}, []
+    embed = (torch.randn(cfg.vocab_size, hid, generator=g) * 0.5).half()
+    tensors["model.embed_tokens.weight"] = embed
+    perm = torch.randperm(cfg.vocab_size, generator=g)
+    head = torch.empty_like(embed)
+    head[perm] = embed
+    tensors["lm_head.weight"] = head
+    tensors["model.norm.weight"] = torch.ones(hid, dtype=torch.float16)
+    for li in range(cfg.num_hidden_layers):
+        p = f"model.layers.{li}."
+        for nm in ("input_layernorm", "post_attention_layernorm"):
+            tensors[p + nm + ".weight"] = (1 + 0.1 * torch.randn(hid, generator=g)).half()
+        for nm in ("self_attn.q_norm", "self_attn.k_norm"):
+            tensors[p + nm + ".weight"] = (1 + 0.1 * torch.randn(d, generator=g)).half()
+        for nm, shape in shapes.items():
+            w = (torch.randn(*shape, generator=g) * 0.05).half()
+            values, scale = rtn_quantize_(w, group_size)
+            tensors[p + nm + ".weight"] = values.contiguous()
+            tensors[p + nm + ".weight.scale"] = scale.contiguous()
+            layers.append(p + nm)
+    save_file(tensors, str(path / "model.safetensors"))
+    config = {f: getattr(cfg, f) for f in cfg.__dataclass_fields__}
+    config["tie_word_embeddings"] = False
+    config["quantization_config"] = {"quant_method": "rtn_w4a16", "bits": 4, "group_size": group_size,
+                                     "symmetric": True}
+    (path / "config.json").write_text(json.dumps(config))
+    (path / "quantized_layers.json").write_text(json.dumps(layers))
+    return path

@@ -1,0 +1,211 @@
+"""The kernel configurations of the benchmark specification at their full sizes.
+
+KV4 (configuration 3): Qwen3-8B attention geometry, batch 1 / 8 / 32 / 64, context
+lengths drawn uniformly from 512..32768, randomly permuted blocks, K/V ~ N(0,1) with
+four outlier channels per head x10 written through the store operator with a static
+per-channel K scale; decode (1 query position) and verify (16 positions, causal over
+the drafts).  The CPU oracle checks a stated subsample of each batch - the longest and
+the shortest sequence plus seeded others, every head - bit for bit for the cache bytes
+and within max-abs-error / RMS <= 1e-2 for the outputs; the remaining sequences are
+covered by a size-independent property (a second run returns identical bits, every
+output is finite and bounded by the largest dequantised value).
+
+W4A16 (configuration 2): the four projection shapes x M in {1, 4, 8, 16, 64, 256, 2048},
+symmetric and affine group-128 quantization, activations with 1 % outlier columns x20,
+max-abs-error / RMS <= 1e-2 against an fp32 matmul on the oracle's dequantised weight.
+"""
+import pytest
+import torch
+
+from oracle import kv4 as ok, w4a16 as ow
+
+pytestmark = pytest.mark.gpu
+
+HQ, HKV, D, PAGE, VGROUP, VERIFY_M = 32, 8, 128, 256, 64, 16
+TOL = 1e-2
+
+
+def err_over_rms(actual, expected):
+    return float((actual - expected).abs().max() / expected.pow(2).mean().sqrt().clamp_min(1e-12))
+
+
+def make_kv(tokens, hkv, seed, channels_k, channels_v):
+    """K, V [tokens, hkv, D] fp16 on the GPU: N(0,1), the given channels of every head x10."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    k = torch.randn(tokens, hkv, D, generator=g, device="cuda")
+    v = torch.randn(tokens, hkv, D, generator=g, device="cuda")
+    for h in range(hkv):
+        k[:, h, channels_k[h].cuda()] *= 10
+        v[:, h, channels_v[h].cuda()] *= 10
+    return k.half(), v.half()
+
+
+def paged_workload(batch, hkv, lo, hi, seed):
+    """Fills a GPU pool through store_kv_quant; returns what decode and verify need plus the
+    subsample for the oracle."""
+    from linkq2_b200.kernels.kv4 import store_kv_quant
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(lo, hi + 1, (batch,), generator=g)
+    if batch > 1:
+        lens[0], lens[1] = hi, lo                      # the extremes are always present
+    else:
+        lens[0] = hi
+    blocks = [(int(l) + PAGE - 1) // PAGE for l in lens]
+    width = max(blocks)
+    n_blocks = sum(blocks) + 3
+    perm = torch.randperm(n_blocks, generator=g).tolist()
+    table = torch.full((batch, width), -1, dtype=torch.int32)
+    at = 0
+    for i, nb in enumerate(blocks):
+        table[i, :nb] = torch.tensor(perm[at:at + nb], dtype=torch.int32)
+        at += nb
+    ck = [torch.randperm(D, generator=g)[:4] for _ in range(hkv)]
+    cv = [torch.randperm(D, generator=g)[:4] for _ in range(hkv)]
+    # pass 1: the static K scale max(amax_t |K|, 1e-4) / 7 over every token of the workload
+    amax = torch.zeros(hkv, D, device="cuda")
+    for i, l in enumerate(lens):
+        k, _ = make_kv(int(l), hkv, seed * 1000 + i, ck, cv)
+        amax = torch.maximum(amax, k.float().abs().amax(0))
+    ks = (amax.clamp_min(1e-4) / 7).half()
+    slots_total = n_blocks * PAGE
+    kq = torch.zeros(slots_total, hkv, D // 8, dtype=torch.uint32, device="cuda")
+    vq = torch.zeros_like(kq)
+    vs = torch.zeros(slots_total, hkv, D // VGROUP, dtype=torch.float16, device="cuda")
+    picked = sorted({0, min(1, batch - 1)} | {int(i) for i in torch.randperm(batch, generator=g)[:2]})
+    sample = {}
+    for i, l in enumerate(lens):
+        l = int(l)
+        k, v = make_kv(l, hkv, seed * 1000 + i, ck, cv)
+        pos = torch.arange(l)
+        slots = (table[i, pos // PAGE].long() * PAGE + pos % PAGE).int()
+        store_kv_quant(k, v, (kq, ks), (vq, vs), slots.cuda(), v_group=VGROUP)
+        if i in picked:
+            sample[i] = (k.cpu(), v.cpu(), slots)
+    torch.cuda.synchronize()
+    return lens, table, (kq, ks), (vq, vs), sample
+
+
+def oracle_subsample(sample, lens, table, k_cache, v_cache, hkv):
+    """CPU pool holding only the sampled sequences (their blocks renumbered from 0), filled by
+    the oracle's store from the same fp16 K/V; the GPU pool's bytes at the real slots must equal
+    it.  Returns the compact pool, tables and lengths for the oracle's attention."""
+    ids = sorted(sample)
+    nb = [(int(lens[i]) + PAGE - 1) // PAGE for i in ids]
+    kc, vc = ok.empty_pool(sum(nb) * PAGE, hkv, D, VGROUP)
+    kc[1].copy_(k_cache[1].cpu())
+    compact = torch.full((len(ids), table.shape[1]), -1, dtype=torch.int32)
+    at = 0
+    for row, (i, n) in enumerate(zip(ids, nb)):
+        compact[row, :n] = torch.arange(at, at + n, dtype=torch.int32)
+        k, v, slots = sample[i]
+        pos = torch.arange(k.shape[0])
+        cslots = (compact[row, pos // PAGE].long() * PAGE + pos % PAGE)
+        ok.store_kv_quant(k, v, kc, vc, cslots, v_group=VGROUP)
+        real = slots.long().cuda()
+        assert torch.equal(k_cache[0].view(torch.int32)[real].cpu(), kc[0][cslots]), "K codes differ"
+        assert torch.equal(v_cache[0].view(torch.int32)[real].cpu(), vc[0][cslots]), "V codes differ"
+        assert torch.equal(v_cache[1][real].cpu(), vc[1][cslots]), "V scales differ"
+        at += n
+    return ids, kc, vc, compact
+
+
+@pytest.mark.parametrize("batch,hkv", [(1, 8), (8, 8), (32, 8), (64, 8), (8, 2), (16, 1)])
+def test_kv4_decode_and_verify_at_specified_sizes(batch, hkv):
+    """hkv 8: the configuration itself (heads per CTA 1, 1, 1, 2; up to 37 KV splits at 32 k
+    capacity); hkv 2 and 1: the per-rank shards of tensor parallelism 4 and 8."""
+    from linkq2_b200.kernels.kv4 import paged_attention_decode
+    hq = HQ * hkv // HKV
+    lens, table, k_cache, v_cache, sample = paged_workload(batch, hkv, 512, 32768, seed=batch * 10 + hkv)
+    ids, kc, vc, compact = oracle_subsample(sample, lens, table, k_cache, v_cache, hkv)
+    bound = float(v_cache[1].float().max()) * 8 * 1.01
+    g = torch.Generator().manual_seed(99)
+    for m in (1, VERIFY_M):
+        ctx = (lens - (m - 1)).int()                   # verify rows read [0, L - 15 + m)
+        q = torch.randn(batch * m, hq, D, generator=g).half()
+        out = paged_attention_decode(q.cuda(), k_cache, v_cache, table.cuda(), ctx.cuda(), block_n=PAGE,
+                                     num_kv_heads=hkv, v_group=VGROUP, verify_m=m)
+        again = paged_attention_decode(q.cuda(), k_cache, v_cache, table.cuda(), ctx.cuda(), block_n=PAGE,
+                                       num_kv_heads=hkv, v_group=VGROUP, verify_m=m)
+        assert torch.equal(out, again)                 # fixed merge order: bits do not depend on timing
+        assert torch.isfinite(out).all() and float(out.float().abs().max()) <= bound
+        rows = torch.cat([torch.arange(i * m, (i + 1) * m) for i in ids])
+        ref = ok.paged_attention_decode(q[rows], kc, vc, compact, ctx[ids], block_n=PAGE, num_kv_heads=hkv,
+                                        v_group=VGROUP, verify_m=m).float()
+        got = out[rows.cuda()].float().cpu()
+        assert err_over_rms(got, ref) <= TOL, (m, err_over_rms(got, ref))
+
+
+@pytest.mark.parametrize("batch", [96, 160])
+def test_kv4_decode_many_short_sequences(batch):
+    """Batches large enough for four and eight KV heads per CTA in the decode kernel's plan."""
+    from linkq2_b200.kernels.kv4 import paged_attention_decode
+    lens, table, k_cache, v_cache, sample = paged_workload(batch, HKV, 64, 1024, seed=batch)
+    ids, kc, vc, compact = oracle_subsample(sample, lens, table, k_cache, v_cache, HKV)
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(batch, HQ, D, generator=g).half()
+    out = paged_attention_decode(q.cuda(), k_cache, v_cache, table.cuda(), lens.int().cuda(), block_n=PAGE,
+                                 num_kv_heads=HKV, v_group=VGROUP)
+    ref = ok.paged_attention_decode(q[ids], kc, vc, compact, lens[ids].int(), block_n=PAGE, num_kv_heads=HKV,
+                                    v_group=VGROUP).float()
+    assert err_over_rms(out[torch.tensor(ids).cuda()].float().cpu(), ref) <= TOL
+
+
+# ---------------------------------------------------------------------------------- W4A16
+SHAPES = [(4096, 6144), (4096, 4096), (4096, 24576), (12288, 4096)]
+ROWS = [1, 4, 8, 16, 64, 256, 2048]
+
+
+def quantized_layer(k, n, affine, seed):
+    """Weight ~ N(0, 0.02^2) drawn and quantized on the GPU with the oracle's formulas
+    (``oracle.w4a16`` is plain torch and runs on any device): the quantizer is not what is
+    under test here, and the large shapes take minutes on host cores."""
+    from linkq2_b200.runtime.backends import make_quant_linear
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).half()
+    if affine:
+        values, scale, zero = ow.affine_quantize(w, 128)
+    else:
+        (values, scale), zero = ow.rtn_quantize(w, 128), None
+    layer = make_quant_linear("b200", values, scale, group_size=128, symmetric=not affine, zero_point=zero,
+                              device="cuda", dtype=torch.float16)
+    dense = ow.dequantize_fp32(values, scale, symmetric=not affine, zero_point=zero)
+    return layer, dense, (values, scale, zero)
+
+
+@pytest.mark.parametrize("k,n", SHAPES)
+@pytest.mark.parametrize("affine", [False, True])
+def test_w4a16_projection_sweep(k, n, affine):
+    layer, dense, (values, scale, zero) = quantized_layer(k, n, affine, seed=k + n + int(affine))
+    # packed words bit-exact against the oracle's closed form (on a slice of the rows for speed)
+    packed, _, _ = ow.runtime_buffers(values[:256].cpu(), scale[:256].cpu(), symmetric=not affine,
+                                      zero_point=None if zero is None else zero[:256].cpu())
+    assert torch.equal(layer.packed[:, :256].cpu(), packed)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    cols = torch.randperm(k, generator=torch.Generator().manual_seed(k))[:max(1, k // 100)]
+    for m in ROWS:
+        x = torch.randn(m, k, generator=g, device="cuda")
+        x[:, cols.cuda()] *= 20                           # 1 % outlier columns
+        x = x.half()
+        y = layer(x).float()
+        expected = x.float() @ dense.t()                  # fp32 matmul on the dequantised weight
+        assert y.shape == (m, n)
+        assert err_over_rms(y, expected) <= TOL, (m, err_over_rms(y, expected))
+        assert float((y - expected).norm() / expected.norm()) < TOL
+
+
+def test_w4a16_config1_gemv():
+    """Configuration 1: K = N = 4096, M = 1, affine group 128, weight N(0, 0.02^2), x ~ N(0,1);
+    packed words bit-exact, output within tolerance of the fp32 oracle (all on host tensors)."""
+    from linkq2_b200.runtime.backends import make_quant_linear
+    w = ow.seeded_weight(4096, 4096, seed=1)
+    values, scale, zero = ow.affine_quantize(w, 128)
+    layer = make_quant_linear("b200", values, scale, group_size=128, symmetric=False, zero_point=zero,
+                              device="cuda", dtype=torch.float16)
+    packed, scales, zeros = ow.runtime_buffers(values, scale, symmetric=False, zero_point=zero)
+    assert torch.equal(layer.packed.cpu(), packed)
+    assert torch.equal(layer.scales.cpu(), scales) and torch.equal(layer.zeros.cpu(), zeros)
+    x = ow.seeded_activation(1, 4096, seed=2)
+    expected = ow.linear_fp32(x, ow.dequantize_fp32(values, scale, symmetric=False, zero_point=zero))
+    y = layer(x.cuda()).float().cpu()
+    assert y.shape == (1, 4096)
+    assert ow.error_over_rms(y, expected) <= TOL

@@ -213,3 +213,31 @@ def test_repeated_block_and_context_swap():
     assert (out2[0].float() - out[0].float()).abs().max().item() > 1e-3
     again = paged_attention_decode(q.cuda(), gk, gv, table.cuda(), lens.cuda(), block_n=page, num_kv_heads=hkv)
     assert torch.equal(out, again)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_store_takes_wider_inputs_at_full_precision(dtype):
+    """The reference's store kernel widens whatever it loads to fp32 (``store.py:31,45``) and its
+    own verify test stores fp32 tensors: fp32 and bf16 inputs are quantized from their own
+    values, bit for bit as the oracle does from ``k.float()``, also from strided slices."""
+    from linkq2_b200.kernels.kv4 import store_kv_quant
+    tokens, h, d, slots_total = 70, 2, 128, 128
+    g = torch.Generator().manual_seed(12)
+    k = (torch.randn(tokens, h, d, generator=g) * 1.7).to(dtype)
+    v = (torch.randn(tokens, h, d, generator=g) * 0.9).to(dtype)
+    ks = ok.static_k_scale(k.float().half())
+    slots = torch.randperm(slots_total, generator=g)[:tokens].int()
+    ref_k, ref_v = ok.empty_pool(slots_total, h, d, 64)
+    ref_k[1].copy_(ks)
+    ok.store_kv_quant(k, v, ref_k, ref_v, slots, v_group=64)
+    for pad in (0, 3):
+        wide = torch.zeros(tokens, 2 * h * d + pad, dtype=dtype, device="cuda")
+        wide[:, :h * d], wide[:, h * d:2 * h * d] = k.cuda().flatten(1), v.cuda().flatten(1)
+        kc, vc = ok.empty_pool(slots_total, h, d, 64)
+        kc[1].copy_(ks)
+        kc, vc = cuda_pool(kc, vc, torch.uint32)
+        store_kv_quant(wide[:, :h * d].unflatten(1, (h, d)), wide[:, h * d:2 * h * d].unflatten(1, (h, d)),
+                       kc, vc, slots.cuda(), v_group=64)
+        assert torch.equal(words(kc[0]), ref_k[0])
+        assert torch.equal(words(vc[0]), ref_v[0])
+        assert torch.equal(vc[1].cpu(), ref_v[1])

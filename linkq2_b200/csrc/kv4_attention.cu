@@ -24,9 +24,6 @@
 // partial (O, max, denominator) per row, takes a ticket, and the last CTA of a
 // (sequence, KV head) merges the partials in split order and writes fp16.
 #include <math.h>
-#ifdef LQ2_TUNING
-#include <stdlib.h>
-#endif
 
 #include <mutex>
 
@@ -419,25 +416,11 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
     return d;
 }
 
-#ifdef LQ2_ATTN_TIMELINE
-__device__ unsigned long long g_attn_timeline[4 * 4096];
-__device__ __forceinline__ void attn_stamp(int slot) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    if (cta < 4096 && threadIdx.x == 0) g_attn_timeline[cta * 4 + slot] = t;
-}
-#define LQ2_ATTN_STAMP(slot) attn_stamp(slot)
-#else
-#define LQ2_ATTN_STAMP(slot) do { } while (0)
-#endif
 
 template <int D, int NG>
 __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const AttnParams p, const int hpc) {
-    LQ2_ATTN_STAMP(0);
     pdl_launch_dependents();
     pdl_wait();
-    LQ2_ATTN_STAMP(1);
     using L = FastLayout<D>;
     constexpr int NW = D / 8;             // words per (token, head)
     constexpr int KWT = NW / 4;           // K words per lane per token
@@ -701,7 +684,6 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
       }
     }
     cp_async_wait<0>();
-    LQ2_ATTN_STAMP(2);
 
     // ---- per-warp results: rows 2t, 2t+1 of 16 * VW * ... dims; denominators summed over the 8 lane groups
 #pragma unroll
@@ -765,7 +747,6 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
             if (d == 0) { __stcg(dst + D, mx); __stcg(dst + D + 1, den); }
         }
     }
-    LQ2_ATTN_STAMP(3);
     if (splits == 1) return;
 
     __threadfence();
@@ -808,9 +789,6 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
 // heads and four splits.  So: the fewest heads per CTA whose grid still fits one wave.
 int fast_heads_per_cta(int batch, int hkv, int64_t capacity) {
     (void)capacity;
-#ifdef LQ2_TUNING
-    if (const char* e = getenv("LQ2_ATTN_HPC")) return atoi(e);
-#endif
     int hpc = 1;
     while (hpc < 8 && hkv % (hpc * 2) == 0 && int64_t(batch) * (hkv / hpc) > 2 * kNumSMs) hpc *= 2;
     return hpc;
@@ -852,9 +830,6 @@ int kv4_attention_splits(int batch, int m, int hq, int hkv, int d, int page, int
     if (splits > most) splits = most;
     if (splits > 64) splits = 64;
     if (splits < 1) splits = 1;
-#ifdef LQ2_TUNING
-    if (const char* e = getenv("LQ2_ATTN_SPLITS")) splits = atoi(e);
-#endif
     return int(splits);
 }
 
@@ -941,10 +916,5 @@ int kv4_attention_launch(const __half* q, int64_t q_stride, const uint32_t* kq, 
 #undef LQ2_ATTN
 }
 
-#ifdef LQ2_ATTN_TIMELINE
-extern "C" int lq2_debug_attn_timeline(unsigned long long* host) {
-    return cudaMemcpyFromSymbol(host, g_attn_timeline, sizeof(unsigned long long) * 4 * 4096) == cudaSuccess ? 0 : 5;
-}
-#endif
 
 }  // namespace lq2

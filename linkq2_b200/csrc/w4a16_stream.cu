@@ -35,16 +35,13 @@
 // the only rounding beyond fp32 accumulation is x/16 for |x| < 2^-10.
 //
 // Split-K.  The CTAs that share a column tile form a thread-block cluster along
-// grid.y.  Each leaves its fp32 partial tile in its own shared memory; after a
-// cluster barrier every CTA sums one slice of the columns over all ranks through
-// distributed shared memory, in rank order (so the result does not depend on
-// timing), and writes fp16.  No global scratch, no atomics.
+// grid.y.  Rank q of the cluster owns a slice of the tile's columns; every rank
+// writes its fp32 partial sums for that slice from registers straight into q's
+// receive area (distributed shared memory stores), one cluster barrier follows, and
+// q adds the parts in rank order (so the result does not depend on timing) and
+// writes fp16.  No global scratch, no atomics.
 #include <cooperative_groups.h>
 #include <cuda.h>
-#ifdef LQ2_TUNING
-#include <cstdio>
-#include <cstdlib>
-#endif
 
 #include "common.cuh"
 
@@ -128,11 +125,7 @@ struct Layout {
     static constexpr int S_BYTES = GPS * TN * 2;
     static constexpr int TX_BYTES = W_BYTES + X_BYTES;          // + S_BYTES (x2 with zero points)
     static constexpr int STAGE_BYTES = (W_BYTES + X_BYTES + 2 * S_BYTES + 1023) / 1024 * 1024;
-#ifdef LQ2_STAGES
-    static constexpr int STAGES = LQ2_STAGES;
-#else
     static constexpr int STAGES = NJ <= 2 ? 4 : 3;
-#endif
     static constexpr int RED_BYTES = MT * TN * 4;               // receive area of the split-K reduction
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
     static constexpr int RECV_OFF = RING_BYTES;                 // never aliased with the ring: peers write into it
@@ -265,9 +258,6 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
             const unsigned char* wsm = base + slab * L::SLAB_BYTES;
             const unsigned char* xsm = base + L::W_BYTES;
             const unsigned char* ssm = xsm + L::X_BYTES + slab * 64 + g * 8;
-#ifdef LQ2_SKIP_COMPUTE
-            if (p.m < 0)
-#endif
 #pragma unroll
             for (int kk = 0; kk < STEPS; ++kk) {
                 const int row = INTERLEAVE ? 8 * (kk >> 1) + 2 * t + (kk & 1) : 4 * kk + t;
@@ -300,7 +290,6 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
                             mma_m16n8k16(gacc[i][j], a0, a1, a2, a3, h ? xb[j].z : xb[j].x, h ? xb[j].w : xb[j].y);
                     }
                 }
-#ifndef LQ2_NO_XSUM
 #pragma unroll
                 for (int j = 0; j < NJW; ++j) {
                     // sum of the step's activations (undoing the 1/16 on the odd slots with 16.0 in A)
@@ -308,7 +297,6 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
                     mma_m16n8k16(xsum[j], kOnes, kOnes, k16s, k16s, xb[j].x, xb[j].y);
                     mma_m16n8k16(xsum[j], kOnes, kOnes, k16s, k16s, xb[j].z, xb[j].w);
                 }
-#endif
                 // end of a scale group, or of this warp's share of one (the scale then multiplies a
                 // partial sum, which is the same by linearity)
                 if ((kk + 1) % (STEPS_PER_GROUP < STEPS ? STEPS_PER_GROUP : STEPS) == 0) {
@@ -467,13 +455,6 @@ Plan make_plan(int m, int n, int k) {
     int r = 1;
     while (r < 8 && base * r * 2 <= resident && stages / (r * 2) >= 2) r *= 2;
     Plan best{nj, wn, m_tiles, n_tiles, r, cdiv(stages, r)};
-#ifdef LQ2_TUNING
-    if (const char* e = getenv("LQ2_W4_PLAN")) {      // "wn,ranks" override for sweeps
-        int wn = 0, r = 0;
-        if (sscanf(e, "%d,%d", &wn, &r) == 2 && (wn == 2 || wn == 4) && r >= 1 && r <= 8 && r <= stages)
-            best = Plan{nj, wn, m_tiles, cdiv(n, 32 * wn), r, cdiv(stages, r)};
-    }
-#endif
     return best;
 }
 
@@ -540,9 +521,6 @@ int launch_one(const W4Params& p, const Plan& pl, cudaStream_t st) {
     size_t smem = L::SMEM_BYTES;
     const int per_sm = cdiv(pl.n_tiles * pl.ranks * pl.m_tiles, kNumSMs);
     constexpr int kResident = NJ <= 2 ? 4 : (NJ == 4 ? 3 : 1);
-#ifdef LQ2_TUNING
-    if (!getenv("LQ2_W4_NOSPREAD"))
-#endif
     if (per_sm < kResident && size_t(227 * 1024 / per_sm - 1024) > smem) smem = size_t(227 * 1024 / per_sm - 1024);
     return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(L::THREADS), smem, st, pl.ranks,
                       map_w, map_x, map_s, map_z, p);

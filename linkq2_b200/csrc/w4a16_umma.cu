@@ -13,12 +13,13 @@
 // Orientation.  The product is computed transposed, Y^T[n, m] = W[n, :] . X[m, :],
 // so that the 128 rows of the MMA are output channels and its N dimension
 // (16..128) is the batch: a 32-row decode batch wastes nothing.  Per CTA: 128
-// output channels x MB batch rows, K streamed in stages of 64.
+// output channels x MB batch rows, K streamed in stages of 128 (64 for batch tiles
+// above 64 rows).
 //
 // Warp roles (10 warps):
-//   warp 0      producer: tiled TMA loads of packed words [8 x 128] int32, the
-//               activation tile [MB x 64] fp16 (128-byte swizzle, K-major: already
-//               the MMA's B operand layout), scales and zero points of the stage
+//   warp 0      producer: tiled TMA loads of the stage's packed words [k/8 x 128]
+//               int32, its activation tile as [MB x 64] fp16 boxes (128-byte swizzle,
+//               K-major: already the MMA's B operand layout), scales and zero points
 //   warps 2-9   dequantise: thread (n, half) turns 4 packed words of channel n into
 //               4 x 8 fp16 values, (u - z) * s rounded once exactly as the reference
 //               (triton_kernels/utils.py:66-71; integer-valued zero points), and
@@ -34,9 +35,6 @@
 // All waits are bounded (see mbar_wait_bounded).
 #include <cooperative_groups.h>
 #include <cuda.h>
-#ifdef LQ2_TUNING
-#include <cstdlib>
-#endif
 #include <algorithm>
 
 #include "common.cuh"
@@ -51,10 +49,7 @@ constexpr int kMaxSmemPerCta = 227 * 1024;
 constexpr int kUM = 128;          // output channels per CTA (MMA M)
 // k per pipeline stage: 128 for batch tiles up to 64 rows (half as many barrier rounds per
 // byte as 64, measured 8-15 % faster), 64 beyond, where the activation tile of a stage grows
-#ifndef LQ2_UMMA_SMALL_STAGE_K
-#define LQ2_UMMA_SMALL_STAGE_K 128
-#endif
-__host__ __device__ constexpr int stage_k(int mb) { return mb <= 64 ? LQ2_UMMA_SMALL_STAGE_K : 64; }
+__host__ __device__ constexpr int stage_k(int mb) { return mb <= 64 ? 128 : 64; }
 constexpr int kUThreads = 320;    // 10 warps
 constexpr int kDequantThreads = 256;
 
@@ -175,11 +170,7 @@ struct ULayout {
     // A tiles in tensor memory.  A 128-k tile takes 64 columns; one of them plus the accumulator
     // fits the 128-column allocation that lets four CTAs share an SM, and the MMAs of a stage
     // are short enough that the next stage's conversion (in registers) hides them.
-#ifdef LQ2_U_ASTAGES
-    static constexpr int A_STAGES = LQ2_U_ASTAGES;
-#else
     static constexpr int A_STAGES = UK == 128 ? 1 : 3;
-#endif
     static constexpr int A_COLS = UK / 2;                           // 32-bit TMEM columns per A tile (two fp16 each)
     static constexpr int XBOX_BYTES = (MB * 128 + 1023) / 1024 * 1024;   // [MB m][64 k] fp16, swizzled
     static constexpr int X_BYTES = (UK / 64) * XBOX_BYTES;
@@ -187,11 +178,7 @@ struct ULayout {
     static constexpr int S_BYTES = GPSU * kUM * 2;                  // [GPSU][128 n] fp16
     static constexpr int RAW_OFF = X_BYTES, S_OFF = RAW_OFF + RAW_BYTES, Z_OFF = S_OFF + S_BYTES;
     static constexpr int R_STAGE_BYTES = (Z_OFF + S_BYTES + 1023) / 1024 * 1024;   // x tile first: 1 KiB aligned
-#ifdef LQ2_U_RSTAGES
-    static constexpr int R_STAGES = LQ2_U_RSTAGES;
-#else
     static constexpr int R_STAGES = UK == 128 ? (MB <= 16 ? 4 : 3) : (MB <= 64 ? 6 : (MB <= 128 ? 4 : 3));
-#endif
     static constexpr int TX_BYTES = (UK / 64) * MB * 128 + RAW_BYTES;   // + S_BYTES (x2 with zero points)
     static constexpr int R_RING_OFF = 0;
     static constexpr int RING_BYTES = R_RING_OFF + R_STAGES * R_STAGE_BYTES;
@@ -212,18 +199,6 @@ struct ULayout {
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
-#ifdef LQ2_U_TIMELINE
-__device__ unsigned long long g_timeline[8 * 4096];
-__device__ __forceinline__ void stamp(int slot) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    if (cta < 4096) g_timeline[cta * 8 + slot] = t;
-}
-#define LQ2_STAMP(slot, cond) do { if (cond) stamp(slot); } while (0)
-#else
-#define LQ2_STAMP(slot, cond) do { } while (0)
-#endif
 
 // CTAs per SM the plan counts on (shared memory and tensor-memory columns allow them; the
 // launch bounds make the register allocation follow)
@@ -235,7 +210,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                   const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                   const UParams p) {
     using L = ULayout<MB, GPSU>;
-    LQ2_STAMP(0, threadIdx.x == 0);                                    // entry
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int RS = L::R_STAGES, AS = L::A_STAGES, UK = L::UK;
@@ -283,7 +257,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     // first half of a cluster barrier: by the time the epilogue waits for it, every CTA of
     // the cluster is known to be running, which remote shared-memory stores require
     if (L::PUSH && ranks > 1) cluster_arrive_release();
-    LQ2_STAMP(1, threadIdx.x == 0);                                    // prologue done
     const uint32_t tmem_base = *tmem_slot;
     unsigned char* r_ring = smem + L::R_RING_OFF;
 
@@ -313,7 +286,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
         if (lane == 0)
             for (int it = 0; it < ahead; ++it) load_weights(it);
         if (p.early_weights) pdl_wait();
-        LQ2_STAMP(2, lane == 0);                                       // previous grid complete
         if (lane == 0)
             for (int it = 0; it < ahead; ++it) load_activations(it);
         __syncwarp();
@@ -387,7 +359,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             const int rslot = U == 1 ? it % RS : us, aslot = it % AS;
             const unsigned char* rbase = r_ring + rslot * L::R_STAGE_BYTES;
             mbar_wait_bounded(raw_full(rslot), U == 1 ? uint32_t(it / RS) & 1u : ring_phase);
-            LQ2_STAMP(3, it == 0 && warp == 2 && lane == 0);           // first stage landed
             const uint32_t* raw = reinterpret_cast<const uint32_t*>(rbase + L::RAW_OFF);
             const __half* sc = reinterpret_cast<const __half*>(rbase + L::S_OFF);
             const __half* zc = reinterpret_cast<const __half*>(rbase + L::Z_OFF);
@@ -442,7 +413,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             mbar_wait_bounded(acc_full, 0);
             tc_fence_after();
         }
-        LQ2_STAMP(4, warp == 2 && lane == 0);                          // all MMAs done
     }
     if constexpr (L::PUSH) {
         // Push: rank q of the cluster owns channels [q * W, (q + 1) * W) of the tile.  Every rank
@@ -478,7 +448,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             cluster_arrive_release();
             cluster_wait_acquire();
         }
-        LQ2_STAMP(5, threadIdx.x == 0);                                // all parts of my slice have arrived
         auto slice_sum = [&](int ml, int col) {
             float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int q = 0; q < ranks; ++q) {
@@ -532,8 +501,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                 }
             }
         }
-        LQ2_STAMP(6, threadIdx.x == 0);                                // output written
-        LQ2_STAMP(7, threadIdx.x == 0);
     } else {
         float* red = reinterpret_cast<float*>(smem);          // [MB][128], in the idle ring
         __syncthreads();                                       // the ring is idle from here on
@@ -557,7 +524,6 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
         __syncthreads();
         if (warp == 1) tmem_dealloc(tmem_base, L::TMEM_COLS);
         if (ranks > 1) cluster.sync();
-        LQ2_STAMP(5, threadIdx.x == 0);                                // partials visible in the cluster
         {
             constexpr int QUADS = kUM / 4;
             const int q0 = rank * QUADS / ranks, q1 = (rank + 1) * QUADS / ranks;
@@ -593,9 +559,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                 }
             }
         }
-        LQ2_STAMP(6, threadIdx.x == 0);                                // output written
         if (ranks > 1) cluster.sync();                                 // nobody leaves while its tile is still being read
-        LQ2_STAMP(7, threadIdx.x == 0);                                // exit
     }
 }
 
@@ -639,9 +603,6 @@ UPlan make_uplan(int m, int n, int k) {
     // 128-row batch tiles at two CTAs per SM beat 256-row tiles at one at every M measured
     // (gate_up geometry: 126 vs 159 us at M = 512, 439 vs 522 us at M = 2048)
     p.mb = m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : 128));
-#ifdef LQ2_TUNING
-    if (const char* e = getenv("LQ2_U_MB")) p.mb = atoi(e);
-#endif
     p.m_tiles = cdiv(m, p.mb);
     p.n_tiles = cdiv(n, kUM);
     const int stages = cdiv(k, stage_k(p.mb));
@@ -649,9 +610,6 @@ UPlan make_uplan(int m, int n, int k) {
     int r = 1;
     const int resident = kNumSMs * resident_ctas(p.mb);
     while (r < 8 && base * r * 2 <= resident && stages / (r * 2) >= 4) r *= 2;
-#ifdef LQ2_TUNING
-    if (const char* e = getenv("LQ2_U_RANKS")) r = atoi(e);
-#endif
     p.ranks = r;
     p.spr = cdiv(stages, r);
     return p;
@@ -687,9 +645,6 @@ int launch_umma(const __half* x, int64_t ldx, const int32_t* packed, const __hal
     size_t smem = L::SMEM_BYTES;
     const int ctas = pl.n_tiles * pl.ranks * pl.m_tiles;
     const int per_sm = cdiv(ctas, kNumSMs);
-#ifdef LQ2_TUNING
-    if (!getenv("LQ2_U_NOSPREAD"))
-#endif
     if (per_sm < resident_ctas(MB)) smem = std::max(smem, size_t(kMaxSmemPerCta / per_sm - 1024));
     return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(kUThreads), smem, st, pl.ranks,
                       map_w, map_x, map_s, map_z, p);

@@ -218,3 +218,58 @@ def test_multi_step_decoding_equals_step_by_step(tmp_path):
     assert got[0] == oracle.greedy(prompts[0], 40, chunk=len(prompts[0]))
     with pytest.raises(ValueError):
         runner.run_steps(seqs, 500)                         # beyond the allocated blocks
+
+
+def test_bench_self_check_on_one_gpu():
+    """The correctness record ``bench.py`` prints at every rank count (a seeded 8-head
+    checkpoint decoded through graphs against ``tests/golden/tp_parity.npz``) must be green
+    on one GPU too, where the same code runs without an exchange."""
+    import bench
+    from linkq2_b200.runtime.parallel import get_tp
+    check = bench.self_check(get_tp(), "cuda:0")
+    assert check["tokens_equal"] is True, check
+    assert check["final_logits_err_over_rms"] < 2e-2
+    assert check["allreduce_timeouts"] == 0 and check["graph_replays"] == 31
+
+
+def test_qwen3_1p7b_width_batch1_matches_oracle(tmp_path):
+    """Configuration 4 in small: Qwen3-1.7B layer width (hidden 2048, intermediate 6144, 16 query
+    and 8 KV heads of 128) with 4 layers and a 4096-token vocabulary, batch 1, CUDA graphs: the
+    batch-1 weight-streaming kernel inside a model.  64 greedy tokens equal the oracle's."""
+    import json
+    from safetensors import safe_open
+    from linkq2_b200.runtime.execute.model_runner import ModelRunner, RunnerConfig
+    from linkq2_b200.runtime.model.qwen3 import ModelConfig
+    from linkq2_b200.runtime.quantization import build_from_checkpoint, save_random_checkpoint
+    from linkq2_b200.runtime.state import BlockPool, Sequence
+    cfg = ModelConfig(vocab_size=4096, hidden_size=2048, intermediate_size=6144, num_hidden_layers=4,
+                      num_attention_heads=16, num_key_value_heads=8, head_dim=128, max_position_embeddings=1024)
+    path = save_random_checkpoint(tmp_path / "w4", cfg, seed=33)
+    weights = {}
+    with safe_open(str(path / "model.safetensors"), framework="pt") as f:
+        for name in json.loads((path / "quantized_layers.json").read_text()):
+            key = name + ".weight"
+            weights[key] = ow.dequantize_fp32(f.get_tensor(key), f.get_tensor(key + ".scale"), symmetric=True)
+        for name in f.keys():
+            if name.endswith(".weight") and name not in weights:
+                weights[name] = f.get_tensor(name)
+    model = build_from_checkpoint(path, device="cuda:0", max_position=1024)
+    rc = RunnerConfig(kvcache_block_size=256, num_kvcache_blocks=4, max_num_seqs=1, max_model_len=512,
+                      enforce_eager=False)
+    shape = (4, 8, 128)
+    runner = ModelRunner(model, rc, smooth_kv={"lambda": torch.ones(shape), "kscale": torch.full(shape, 0.5)},
+                         device="cuda:0")
+    g = torch.Generator().manual_seed(2)
+    prompt = torch.randint(0, 4095, (48,), generator=g).tolist()
+    seq = Sequence(prompt, 256)
+    BlockPool(4).ensure(seq, 48 + 64 + 1)
+    tokens = runner.run([seq], True)
+    seq.append(tokens[0])
+    tokens += [row[0] for row in runner.run_steps([seq], 63)]
+    oracle = oq.OracleQwen3(cfg, weights, kscale=torch.full(shape, 0.5), max_tokens=256)
+    assert tokens == oracle.greedy(prompt, 64)
+    assert len(set(tokens)) > 8
+    expected = oracle.last_logits[-1]
+    got = runner.last_logits.float().cpu()[0]
+    assert (got - expected).abs().max() / expected.pow(2).mean().sqrt() < 2e-2
+    runner.shutdown()

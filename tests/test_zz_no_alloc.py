@@ -36,11 +36,11 @@ def _case(bs, lens, m, hq, hkv, d, page, seed):
     return kc, vc, table, torch.tensor(lens, dtype=torch.int32), q
 
 
-def _static_call(q, kc, vc, table, lens, m, hkv, page):
+def _static_call(q, kc, vc, table, lens, m, hkv, page, out=None):
     """Raw ctypes call: pointers, sizes and the current stream; no workspace."""
     from linkq2_b200 import _lib
     rows, hq, d = q.shape
-    out = torch.empty_like(q)
+    out = torch.empty_like(q) if out is None else out
     status = _lib.lib.lq2_kv4_attention_static(
         q.data_ptr(), q.stride(0), kc[0].data_ptr(), kc[1].data_ptr(), vc[0].data_ptr(), vc[1].data_ptr(),
         table.data_ptr(), lens.data_ptr(), out.data_ptr(), rows // m, m, hq, hkv, d, page, table.shape[1],
@@ -60,13 +60,18 @@ def test_static_scratch_matches_workspace_entry_twice(bs, lens, m):
     table, ctx, q = table.cuda(), ctx.cuda(), q.cuda()
     expected = paged_attention_decode(q, gk, gv, table, ctx, block_n=page, num_kv_heads=hkv, verify_m=m)
     before = torch.cuda.memory_allocated()
-    for _ in range(2):
-        status, out = _static_call(q, gk, gv, table, ctx, m, hkv, page)
+    for call in range(2):
+        out = torch.empty_like(q)                            # the caller's output, allocated before the call
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]           # device-wide free bytes (cudaMemGetInfo)
+        status, out = _static_call(q, gk, gv, table, ctx, m, hkv, page, out)
         assert status == _lib.OK
         torch.cuda.synchronize()
+        if call == 1:                                        # the first call on a device may load the module
+            assert torch.cuda.mem_get_info()[0] == free_before, "the call changed the device's free memory"
         assert (out.float() - expected.float()).abs().max().item() < ATOL
     del out
-    assert torch.cuda.memory_allocated() == before           # nothing was taken from torch's pool
+    assert torch.cuda.memory_allocated() == before           # nothing was taken from torch's pool either
     ref = ok.paged_attention_decode(q.cpu(), kc, vc, table.cpu(), ctx.cpu(), block_n=page, num_kv_heads=hkv,
                                     verify_m=m)
     assert (expected.float().cpu() - ref.float()).abs().max().item() < ATOL

@@ -88,6 +88,9 @@ GEOMETRY = {
     "1p7b": dict(vocab_size=151936, hidden_size=2048, intermediate_size=6144, num_hidden_layers=28,
                  num_attention_heads=16, num_key_value_heads=8, head_dim=128, max_position_embeddings=40960,
                  tie_word_embeddings=True),
+    "1p7b_permuted_head": dict(vocab_size=151936, hidden_size=2048, intermediate_size=6144, num_hidden_layers=28,
+                               num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                               max_position_embeddings=40960, tie_word_embeddings=False),
 }
 
 
@@ -107,8 +110,21 @@ def build_checkpoint(geometry: str, layers: int | None, work: Path, seed: int = 
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     with torch.device(dev):
         hf = Qwen3ForCausalLM(cfg).half().eval()
+    g = torch.Generator().manual_seed(seed + 1)
     with torch.no_grad():
-        hf.lm_head.weight = hf.model.embed_tokens.weight
+        if kw["tie_word_embeddings"]:
+            hf.lm_head.weight = hf.model.embed_tokens.weight
+        else:
+            # Random-init layers give nearly flat logits whose arg-max is decided by rounding noise in any
+            # implementation.  A larger embedding and a head that is a row permutation of it make greedy
+            # decoding walk through the vocabulary with margins that numerics cannot flip, while attention
+            # and the MLPs still shape the logits (compared numerically as well).
+            embed = (torch.randn(kw["vocab_size"], kw["hidden_size"], generator=g) * 0.25).half()
+            perm = torch.randperm(kw["vocab_size"], generator=g)
+            head = torch.empty_like(embed)
+            head[perm] = embed
+            hf.model.embed_tokens.weight.copy_(embed)
+            hf.lm_head.weight.copy_(head)
     source, quantized = work / "fp16", work / "w4"
     hf.save_pretrained(source)
     artifact = quantize_model(hf, CompressionConfig(group_size=128, device=dev))
@@ -187,7 +203,10 @@ def section_tokens(args):
     import tempfile
     import torch
     prepare()
-    for geometry, layers, prompt_len, new_tokens in (("tiny", None, 40, 64), ("1p7b", args.layers, 512, 256)):
+    cases = (("tiny", None, 40, 64), ("1p7b", args.layers, 512, 256), ("1p7b_permuted_head", args.layers, 512, 256))
+    for geometry, layers, prompt_len, new_tokens in cases:
+        if args.only and geometry != args.only:
+            continue
         rec = {"geometry": geometry, "prompt_tokens": prompt_len, "new_tokens": new_tokens}
         try:
             with tempfile.TemporaryDirectory() as tmp:
@@ -387,6 +406,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("section", choices=["tests", "tokens", "store", "kernels", "all"])
     ap.add_argument("--layers", type=int, default=None, help="decoder layers of the 1.7B-geometry checkpoint (default 28)")
+    ap.add_argument("--only", default=None, help="tokens: run this geometry only")
     args = ap.parse_args()
     if not (HERE / "_ref" / "qslab").exists():
         emit(args.section, {"error": "baseline/_ref is missing: run baseline/install_reference.sh first"})

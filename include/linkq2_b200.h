@@ -177,8 +177,9 @@ size_t lq2_kv4_attention_workspace_bytes(int batch, int verify_m, int hq, int hk
  *                 positions [0, context_lens[seq] + m) capped at max_blocks*page
  *   out           [batch*verify_m, HQ, D] fp16 contiguous
  * Positions under a negative block-table entry are masked; a row without any
- * valid position yields zeros.  Block ids are clamped into the pool
- * ([0, num_slots/page)) before any address is formed.
+ * valid position yields zeros.  Block ids are clamped into the pool's whole pages
+ * ([0, floor(num_slots/page)); the pool need not be a multiple of the page, as the
+ * reference's own tests allocate it) before any address is formed.
  * D must be 64 or 128, HQ a multiple of HKV with verify_m*HQ/HKV <= 64,
  * page a multiple of 16.
  */

@@ -190,7 +190,7 @@ int lq2_kv4_attention(const void* q, int64_t q_row_stride, const uint32_t* kq, c
     if (!q || !kq || !ks || !vq || !vs || !block_tables || !context_lens || !out || num_slots <= 0)
         return LQ2_ERR_ARG;
     if (!attn_shape_ok(batch, verify_m, hq, hkv, d, page, max_blocks)) return LQ2_ERR_SHAPE;
-    if (v_group < d / 8 || !pow2(v_group) || d % v_group || num_slots % page) return LQ2_ERR_SHAPE;
+    if (v_group < d / 8 || !pow2(v_group) || d % v_group || num_slots < page) return LQ2_ERR_SHAPE;
     if (!aligned(kq, 16) || !aligned(vq, 16) || !aligned(q, 2) || !aligned(workspace, 16)) return LQ2_ERR_ALIGN;
     return kv4_attention_launch(static_cast<const __half*>(q), q_row_stride, kq,
                                 static_cast<const __half*>(ks), vq, static_cast<const __half*>(vs),
@@ -208,7 +208,7 @@ int lq2_kv4_attention_static(const void* q, int64_t q_row_stride, const uint32_t
                              void* stream) {
     if (batch == 0) return LQ2_OK;
     if (!attn_shape_ok(batch, verify_m, hq, hkv, d, page, max_blocks)) return LQ2_ERR_SHAPE;
-    if (v_group < d / 8 || !pow2(v_group) || d % v_group || num_slots <= 0 || num_slots % page) return LQ2_ERR_SHAPE;
+    if (v_group < d / 8 || !pow2(v_group) || d % v_group || num_slots < page) return LQ2_ERR_SHAPE;
     const size_t need = kv4_attention_workspace_bytes(batch, verify_m, hq, hkv, d, page, max_blocks);
     if (need > kv4_attention_builtin_scratch_bytes()) return LQ2_ERR_LIMIT;
     if (!q || !kq || !ks || !vq || !vs || !block_tables || !context_lens || !out) return LQ2_ERR_ARG;

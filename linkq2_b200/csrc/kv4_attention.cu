@@ -657,11 +657,14 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
                 for (int q = 0; q < NG; ++q) {
                     const float fa = __half2float(__ushort_as_half((unsigned short)(q ? (sA >> 16) : (sA & 0xffff))));
                     const float fb = __half2float(__ushort_as_half((unsigned short)(q ? (sB >> 16) : (sB & 0xffff))));
-                    const float e0 = p0 * fa, e1 = p1 * fa, e2 = p2 * fb, e3 = p3 * fb;
-                    lp[q][0] += e0 + e2;
-                    lp[q][1] += e1 + e3;
-                    const uint32_t b0 = movmatrix_trans(pack_h2(e0, e1));
-                    const uint32_t b1 = movmatrix_trans(pack_h2(e2, e3));
+                    // P' is rounded to fp16 for the MMA; the offset term -8 * sum P' must use the same
+                    // rounded values, or the rounding noise would enter the result multiplied by 8
+                    const uint32_t h01 = pack_h2(p0 * fa, p1 * fa), h23 = pack_h2(p2 * fb, p3 * fb);
+                    const float2 r01 = __half22float2(u32_as_h2(h01)), r23 = __half22float2(u32_as_h2(h23));
+                    lp[q][0] += r01.x + r23.x;
+                    lp[q][1] += r01.y + r23.y;
+                    const uint32_t b0 = movmatrix_trans(h01);
+                    const uint32_t b1 = movmatrix_trans(h23);
 #pragma unroll
                     for (int wsel = (NG == 2 ? q : 0); wsel < (NG == 2 ? q + 1 : VW); ++wsel) {
                         const int wo = (wsel * 8 + g) * 4;

@@ -274,8 +274,8 @@ class ModelRunner:
         base = np.array([len(seq) for seq in seqs], dtype=np.int64)
         tables = np.full((b, width), -1, dtype=np.int32)
         for i, seq in enumerate(seqs):
-            n = min(len(seq.block_table), width)
-            tables[i, :n] = seq.block_table[:n]
+            held = min(len(seq.block_table), width)
+            tables[i, :held] = seq.block_table[:held]
         bs = self.block_size
         for i in range(steps):
             pos = base - 1 + i

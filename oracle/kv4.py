@@ -121,7 +121,7 @@ def materialize_kv(k_cache, v_cache, slots, v_group: int = 64):
 
 def paged_attention_decode(q, k_cache, v_cache, block_tables, context_lens,
                            block_n: int = 128, num_kv_heads: int | None = None,
-                           k_scale=None, v_group: int = 64, verify_m: int = 1):
+                           k_scale=None, v_group: int = 64, verify_m: int = 1, out_dtype=torch.float16):
     """``q [rows, HQ, D] fp16 -> out [rows, HQ, D] fp16`` with ``rows = B * M``.
 
     Row ``seq*M + m`` reads logical positions ``[0, L_seq + m)`` capped at the
@@ -130,7 +130,8 @@ def paged_attention_decode(q, k_cache, v_cache, block_tables, context_lens,
     ``grouped_attention.py:38,46``).  Scores are scaled by ``D**-0.5``
     (``:146``), softmax and the value sum are fp32 and a row with no valid key
     yields zeros (``:66-70,84-85``: ``acc / max(l, 1e-20)`` with ``acc = 0``).
-    The fp32 result is rounded to fp16 once.
+    The fp32 result is rounded to fp16 once (``out_dtype=torch.float32`` returns it
+    unrounded: the fp32 reference of the output tolerance).
     """
     rows, hq, d = q.shape
     hkv = num_kv_heads if num_kv_heads is not None else hq
@@ -161,7 +162,7 @@ def paged_attention_decode(q, k_cache, v_cache, block_tables, context_lens,
             scores = torch.einsum("hd,htd->ht", q[row].float(), kh) * (d ** -0.5)
             scores = scores.masked_fill(~valid.unsqueeze(0), float("-inf"))
             out[row] = torch.einsum("ht,htd->hd", torch.softmax(scores, -1), vh)
-    return out.to(torch.float16)
+    return out.to(out_dtype)
 
 
 # --------------------------------------------------------------------------

@@ -68,7 +68,7 @@ def test_static_scratch_matches_workspace_entry_twice(bs, lens, m):
         assert status == _lib.OK
         torch.cuda.synchronize()
         if call == 1:                                        # the first call on a device may load the module
-            assert torch.cuda.mem_get_info()[0] == free_before, "the call changed the device's free memory"
+            assert torch.cuda.mem_get_info()[0] >= free_before, "the call took device memory"
         assert (out.float() - expected.float()).abs().max().item() < ATOL
     del out
     assert torch.cuda.memory_allocated() == before           # nothing was taken from torch's pool either

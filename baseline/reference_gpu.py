@@ -119,12 +119,15 @@ def build_checkpoint(geometry: str, layers: int | None, work: Path, seed: int = 
             # implementation.  A larger embedding and a head that is a row permutation of it make greedy
             # decoding walk through the vocabulary with margins that numerics cannot flip, while attention
             # and the MLPs still shape the logits (compared numerically as well).
-            embed = (torch.randn(kw["vocab_size"], kw["hidden_size"], generator=g) * 0.25).half()
+            embed = (torch.randn(kw["vocab_size"], kw["hidden_size"], generator=g) * 0.5).half()
             perm = torch.randperm(kw["vocab_size"], generator=g)
             head = torch.empty_like(embed)
             head[perm] = embed
             hf.model.embed_tokens.weight.copy_(embed)
             hf.lm_head.weight.copy_(head)
+            for name, param in hf.named_parameters():       # small residual branches: the embedding stays dominant
+                if name.endswith(("o_proj.weight", "down_proj.weight")):
+                    param.mul_(0.05)
     source, quantized = work / "fp16", work / "w4"
     hf.save_pretrained(source)
     artifact = quantize_model(hf, CompressionConfig(group_size=128, device=dev))

@@ -87,6 +87,12 @@ __device__ __forceinline__ void ldg(uint2& d, const uint32_t* p) { d = ldg_strea
 __device__ __forceinline__ void ldg(uint32_t& d, const uint32_t* p) { d = ldg_stream_u1(p); }
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) { return h2_as_u32(__floats2half2_rn(a, b)); }
+// 2^x for x <= 0 (or -inf): the hardware approximation, 2 ulp
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // RT: 16-row query tiles per (sequence, KV head): ceil(M * rep / 16), 3 rounded up to 4.
 template <int D, int RT>
@@ -362,6 +368,285 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
 }
 
 // =====================================================================================
+// Verify path: 17..64 query rows per KV head (M draft positions x the GQA group), D = 128.
+//
+// Replaces kv4_grouped_verify_kernel (qslab/kernels/kv4/grouped_attention.py:7-63), which
+// dequantises every K/V tile once per 16-row query block.  Here the CTA of one (sequence, KV
+// head, split) dequantises each 32-token tile ONCE, cooperatively, into shared memory as
+// fp16 - K as the exact integers (nibble - 8), the static K scale being folded into Q'; V as
+// fp16((nibble - 8) * vs), the rounding of the reference's kernel (:50-53) - and every warp
+// (one 16-row query tile each) reads its MMA operands from there with ldmatrix.  The packed
+// words of the next tile are in flight (registers) while the current one is multiplied, and
+// the two shared-memory buffers alternate, so there is one CTA barrier per tile.
+// Within every 8 channels the tile keeps the order the nibble masks produce, (0,4,1,5,2,6,3,7);
+// Q' is loaded in the same order and O is put back in natural order at the write-out.
+// =====================================================================================
+constexpr int kVTile = 32;                 // tokens per tile
+constexpr int kVStride = 128 + 8;          // halves per token row: +16 bytes keep ldmatrix conflict-free
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem_row) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* smem_row) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+
+template <int RT>
+__global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParams p) {
+    pdl_launch_dependents();
+    pdl_wait();
+    constexpr int D = 128, NW = 16;
+    __shared__ __align__(16) __half sm_k[2][kVTile * kVStride];
+    __shared__ __align__(16) __half sm_v[2][kVTile * kVStride];
+    __shared__ int s_ticket;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    const int rep = p.hq / p.hkv;
+    const int rows_valid = p.m * rep;
+
+    const int capacity = p.max_blocks * p.page;
+    const int len = p.lens[seq];
+    const int reach = min(len + p.m - 1, capacity);
+    const int tiles = reach > 0 ? (reach + kVTile - 1) / kVTile : 0;
+    const int per_split = (tiles + p.splits - 1) / p.splits;
+    const int tile_begin = split * per_split;
+    const int tile_end = min(tiles, tile_begin + per_split);
+
+    // ---- Q' fragments of this warp's row tile (A operand, 8 k-chunks of 16 channels, stored order)
+    const bool mma_warp = warp < RT;
+    const int r_lo = 16 * warp + g, r_hi = r_lo + 8;
+    const bool v_lo = mma_warp && r_lo < rows_valid, v_hi = mma_warp && r_hi < rows_valid;
+    const int m_lo = v_lo ? r_lo / rep : 0, m_hi = v_hi ? r_hi / rep : 0;
+    const int lim_lo = v_lo ? min(len + m_lo, capacity) : 0;
+    const int lim_hi = v_hi ? min(len + m_hi, capacity) : 0;
+    uint32_t qa[8][4];
+    {
+        const __half* q_lo = p.q + int64_t(seq * p.m + m_lo) * p.q_stride + (kvh * rep + (v_lo ? r_lo % rep : 0)) * D;
+        const __half* q_hi = p.q + int64_t(seq * p.m + m_hi) * p.q_stride + (kvh * rep + (v_hi ? r_hi % rep : 0)) * D;
+        const __half* ksp = p.ks + kvh * D;
+#pragma unroll
+        for (int kc = 0; kc < 8; ++kc) {
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                // stored positions 2t, 2t+1 of an 8-channel chunk are the natural channels t and t + 4
+                const int d0 = 16 * kc + 8 * hf + t, d1 = d0 + 4;
+                const float s0 = __half2float(ksp[d0]), s1 = __half2float(ksp[d1]);
+                qa[kc][2 * hf] = pack_h2(v_lo ? __half2float(q_lo[d0]) * s0 : 0.f, v_lo ? __half2float(q_lo[d1]) * s1 : 0.f);
+                qa[kc][2 * hf + 1] = pack_h2(v_hi ? __half2float(q_hi[d0]) * s0 : 0.f, v_hi ? __half2float(q_hi[d1]) * s1 : 0.f);
+            }
+        }
+    }
+
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[j][c] = 0.f;
+    float mx_lo = -INFINITY, mx_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+
+    // ---- cooperative dequantisation: thread (token = tid / 4, quarter = tid % 4) owns 4 K and 4 V words
+    const int dq_tok = tid >> 2, dq_q = tid & 3;
+    const __half2 k1032 = __floats2half2_rn(1032.f, 1032.f);
+    const __half2 k16th = __floats2half2_rn(0.0625f, 0.0625f);
+    const __half2 km72 = __floats2half2_rn(-72.f, -72.f);
+    const int vgrp = (32 * dq_q) >> p.vg_shift;
+    uint4 kw, vw;
+    __half vsc = __float2half_rn(0.f);
+    bool live = false;
+
+    auto fetch = [&](int tile) {
+        const int pos0 = tile * kVTile;
+        const int raw = p.bt[int64_t(seq) * p.max_blocks + pos0 / p.page];
+        live = raw >= 0;                                          // a tile never straddles pages (page % 32 == 0)
+        if (!live) return;
+        const int blk = min(raw, p.num_blocks - 1);
+        const int64_t slot = int64_t(blk) * p.page + pos0 % p.page + dq_tok;
+        kw = ldg_stream_u4(p.kq + (slot * p.hkv + kvh) * NW + 4 * dq_q);
+        vw = ldg_stream_u4(p.vq + (slot * p.hkv + kvh) * NW + 4 * dq_q);
+        vsc = p.vs[(slot * p.hkv + kvh) * p.ng + vgrp];
+    };
+    auto convert = [&](int buf) {                                 // registers -> fp16 rows of buffer `buf`
+        const uint32_t kws[4] = {kw.x, kw.y, kw.z, kw.w}, vws[4] = {vw.x, vw.y, vw.z, vw.w};
+        const __half2 sc2 = __half2half2(vsc);
+        __half* kdst = sm_k[buf] + dq_tok * kVStride + 32 * dq_q;
+        __half* vdst = sm_v[buf] + dq_tok * kVStride + 32 * dq_q;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t a = kws[i], a8 = a >> 8, b = vws[i], b8 = b >> 8;
+            uint4 ko, vo;
+            // (n0,n4) (n1,n5) (n2,n6) (n3,n7) as exact integers (nibble - 8)
+            ko.x = h2_as_u32(__hsub2(u32_as_h2(and_or(a, 0x000f000fu, 0x64006400u)), k1032));
+            ko.y = h2_as_u32(__hfma2(u32_as_h2(and_or(a, 0x00f000f0u, 0x64006400u)), k16th, km72));
+            ko.z = h2_as_u32(__hsub2(u32_as_h2(and_or(a8, 0x000f000fu, 0x64006400u)), k1032));
+            ko.w = h2_as_u32(__hfma2(u32_as_h2(and_or(a8, 0x00f000f0u, 0x64006400u)), k16th, km72));
+            vo.x = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(b, 0x000f000fu, 0x64006400u)), k1032), sc2));
+            vo.y = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(b, 0x00f000f0u, 0x64006400u)), k16th, km72), sc2));
+            vo.z = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(b8, 0x000f000fu, 0x64006400u)), k1032), sc2));
+            vo.w = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(b8, 0x00f000f0u, 0x64006400u)), k16th, km72), sc2));
+            *reinterpret_cast<uint4*>(kdst + 8 * i) = ko;
+            *reinterpret_cast<uint4*>(vdst + 8 * i) = vo;
+        }
+    };
+
+    bool cur_live = false;
+    if (tile_begin < tile_end) {
+        fetch(tile_begin);
+        cur_live = live;
+        if (live) convert(0);
+    }
+    __syncthreads();
+    for (int tile = tile_begin; tile < tile_end; ++tile) {
+        const int buf = (tile - tile_begin) & 1;
+        const bool has_next = tile + 1 < tile_end;
+        if (has_next) fetch(tile + 1);                            // in flight during the MMAs below
+        const bool next_live = has_next && live;
+        if (cur_live && mma_warp) {
+            const __half* kb = sm_k[buf];
+            const __half* vb = sm_v[buf];
+            // ---- S = Q' K^T: 16 rows x 32 tokens
+            float s[4][4];
+#pragma unroll
+            for (int n8 = 0; n8 < 4; ++n8) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) s[n8][c] = 0.f;
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {                  // 32 channels: two k-chunks per ldmatrix
+                    uint32_t bf[4];
+                    ldsm_x4(bf, kb + (8 * n8 + (lane & 7)) * kVStride + (4 * q4 + (lane >> 3)) * 8);
+                    mma_m16n8k16(s[n8], qa[2 * q4][0], qa[2 * q4][1], qa[2 * q4][2], qa[2 * q4][3], bf[0], bf[1]);
+                    mma_m16n8k16(s[n8], qa[2 * q4 + 1][0], qa[2 * q4 + 1][1], qa[2 * q4 + 1][2], qa[2 * q4 + 1][3], bf[2], bf[3]);
+                }
+            }
+            // ---- mask, online softmax (base-2 domain)
+            const int pos0 = tile * kVTile;
+            float t_lo = -INFINITY, t_hi = -INFINITY;
+#pragma unroll
+            for (int n8 = 0; n8 < 4; ++n8) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int pos = pos0 + 8 * n8 + 2 * t + (c & 1);
+                    const int lim = c < 2 ? lim_lo : lim_hi;
+                    const float v = pos < lim ? s[n8][c] * p.sl2 : -INFINITY;
+                    s[n8][c] = v;
+                    if (c < 2) t_lo = fmaxf(t_lo, v); else t_hi = fmaxf(t_hi, v);
+                }
+            }
+            t_lo = fmaxf(t_lo, __shfl_xor_sync(0xffffffffu, t_lo, 1));
+            t_lo = fmaxf(t_lo, __shfl_xor_sync(0xffffffffu, t_lo, 2));
+            t_hi = fmaxf(t_hi, __shfl_xor_sync(0xffffffffu, t_hi, 1));
+            t_hi = fmaxf(t_hi, __shfl_xor_sync(0xffffffffu, t_hi, 2));
+            const float n_lo = fmaxf(mx_lo, t_lo), n_hi = fmaxf(mx_hi, t_hi);
+            const float safe_lo = n_lo == -INFINITY ? 0.f : n_lo;
+            const float safe_hi = n_hi == -INFINITY ? 0.f : n_hi;
+            const float a_lo = ex2(mx_lo - safe_lo), a_hi = ex2(mx_hi - safe_hi);
+            mx_lo = n_lo;
+            mx_hi = n_hi;
+            float sum_lo = 0.f, sum_hi = 0.f;
+#pragma unroll
+            for (int n8 = 0; n8 < 4; ++n8) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const float e = ex2(s[n8][c] - (c < 2 ? safe_lo : safe_hi));
+                    s[n8][c] = e;
+                    if (c < 2) sum_lo += e; else sum_hi += e;
+                }
+            }
+            l_lo = l_lo * a_lo + sum_lo;
+            l_hi = l_hi * a_hi + sum_hi;
+            if (__any_sync(0xffffffffu, a_lo != 1.f || a_hi != 1.f)) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    o[j][0] *= a_lo; o[j][1] *= a_lo;
+                    o[j][2] *= a_hi; o[j][3] *= a_hi;
+                }
+            }
+            // ---- O += P V: two k-chunks of 16 tokens, 16 blocks of 8 channels
+#pragma unroll
+            for (int c16 = 0; c16 < 2; ++c16) {
+                const uint32_t pa0 = pack_h2(s[2 * c16][0], s[2 * c16][1]), pa1 = pack_h2(s[2 * c16][2], s[2 * c16][3]);
+                const uint32_t pa2 = pack_h2(s[2 * c16 + 1][0], s[2 * c16 + 1][1]), pa3 = pack_h2(s[2 * c16 + 1][2], s[2 * c16 + 1][3]);
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {                  // two channel blocks per ldmatrix
+                    uint32_t bf[4];
+                    ldsm_x4_trans(bf, vb + (16 * c16 + 8 * ((lane >> 3) & 1) + (lane & 7)) * kVStride + (2 * jj + (lane >> 4)) * 8);
+                    mma_m16n8k16(o[2 * jj], pa0, pa1, pa2, pa3, bf[0], bf[1]);
+                    mma_m16n8k16(o[2 * jj + 1], pa0, pa1, pa2, pa3, bf[2], bf[3]);
+                }
+            }
+        }
+        if (next_live) convert(buf ^ 1);
+        cur_live = next_live;
+        __syncthreads();
+    }
+
+    // ---- write-out.  o[j][0..1] is (row r_lo, stored columns 8j + 2t, 8j + 2t + 1) = natural channels
+    // 8j + t and 8j + t + 4; o[j][2..3] the same for r_hi.
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+    const int splits = p.splits;
+    float* part = p.partial + (int64_t(seq * p.hkv + kvh) * splits) * rows_valid * (D + 2);
+    if (mma_warp) {
+#pragma unroll
+        for (int hfr = 0; hfr < 2; ++hfr) {
+            const int row = hfr ? r_hi : r_lo;
+            if (row >= rows_valid) continue;
+            const float den = hfr ? l_hi : l_lo, mx = hfr ? mx_hi : mx_lo;
+            if (splits == 1) {
+                const float inv = 1.f / fmaxf(den, 1e-20f);
+                __half* dst = p.out + (int64_t(seq * p.m + row / rep) * p.hq + kvh * rep + row % rep) * D;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    dst[8 * j + t] = __float2half_rn(o[j][2 * hfr] * inv);
+                    dst[8 * j + t + 4] = __float2half_rn(o[j][2 * hfr + 1] * inv);
+                }
+            } else {
+                float* dst = part + (int64_t(split) * rows_valid + row) * (D + 2);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    __stcg(dst + 8 * j + t, o[j][2 * hfr]);
+                    __stcg(dst + 8 * j + t + 4, o[j][2 * hfr + 1]);
+                }
+                if (t == 0) { __stcg(dst + D, mx); __stcg(dst + D + 1, den); }
+            }
+        }
+    }
+    if (splits == 1) return;
+
+    __threadfence();
+    __syncthreads();
+    int* counter = p.counters + seq * p.hkv + kvh;
+    if (tid == 0) s_ticket = atomicAdd(counter, 1);
+    __syncthreads();
+    if (s_ticket != splits - 1) return;
+    __threadfence();
+    for (int e = tid; e < rows_valid * D; e += kThreads) {
+        const int row = e / D, d = e % D;
+        float mx = -INFINITY;
+        for (int sp = 0; sp < splits; ++sp)
+            mx = fmaxf(mx, __ldcg(part + (int64_t(sp) * rows_valid + row) * (D + 2) + D));
+        const float safe = mx == -INFINITY ? 0.f : mx;
+        float acc = 0.f, den = 0.f;
+        for (int sp = 0; sp < splits; ++sp) {
+            const float* src = part + (int64_t(sp) * rows_valid + row) * (D + 2);
+            const float f = ex2(__ldcg(src + D) - safe);
+            acc += __ldcg(src + d) * f;
+            den += __ldcg(src + D + 1) * f;
+        }
+        const int mrow = row / rep, head = kvh * rep + row % rep;
+        p.out[(int64_t(seq * p.m + mrow) * p.hq + head) * D + d] = __float2half_rn(acc / fmaxf(den, 1e-20f));
+    }
+    if (tid == 0) *counter = 0;
+}
+
+// =====================================================================================
 // Fast decode path: at most 8 query rows per KV head (one decode position of a GQA group
 // of up to 8 heads, or a few verify positions), D in {64, 128}, at most two V groups.
 //
@@ -404,12 +689,6 @@ __device__ __forceinline__ void cp_async_16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
-// 2^x for x <= 0 (or -inf): the hardware approximation, 2 ulp
-__device__ __forceinline__ float ex2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
-    return y;
-}
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
     uint32_t d;
     asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(d) : "r"(a));
@@ -644,6 +923,12 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
 #pragma unroll
                 for (int j = 0; j < NO; ++j) { o[j][0] *= a0; o[j][1] *= a1; o[j][2] *= a0; o[j][3] *= a1; }
             }
+            // The codes enter the MMAs as unsigned values, so the raw sums are large and positive while the
+            // result (after the -8 * sum P' term) is small.  The tensor core truncates when it adds into its
+            // accumulator; adding every tile into one long-lived accumulator would turn that into a bias that
+            // grows with the context.  Each tile therefore starts fresh accumulators, which are added to the
+            // running sums with ordinary (round-to-nearest) fp32 additions.
+            float ot[NO][4];
 #pragma unroll
             for (int b16 = 0; b16 < 2; ++b16) {
                 const float p0 = ex2(sv[b16][0] - safe0), p1 = ex2(sv[b16][1] - safe1);
@@ -676,12 +961,20 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
                         for (int b = 0; b < 4; ++b) {
                             const uint32_t sel = b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12);
                             const uint32_t xa = __byte_perm(w0, w1, sel), xb = __byte_perm(w2, w3, sel);
-                            mma_m16n8k16(o[wsel * 4 + b], xa & 0x000f000fu, xa & 0x00f000f0u, xb & 0x000f000fu,
-                                         xb & 0x00f000f0u, b0, b1);
+                            if (b16 == 0)
+                                mma_m16n8k16_zero(ot[wsel * 4 + b], xa & 0x000f000fu, xa & 0x00f000f0u, xb & 0x000f000fu,
+                                                  xb & 0x00f000f0u, b0, b1);
+                            else
+                                mma_m16n8k16(ot[wsel * 4 + b], xa & 0x000f000fu, xa & 0x00f000f0u, xb & 0x000f000fu,
+                                             xb & 0x00f000f0u, b0, b1);
                         }
                     }
                 }
             }
+#pragma unroll
+            for (int j = 0; j < NO; ++j)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) o[j][c] += ot[j][c];
         }
         __syncwarp();
       }
@@ -910,6 +1203,10 @@ int kv4_attention_launch(const __half* q, int64_t q_stride, const uint32_t* kq, 
     }
     const int rt = row_tiles(m, hq, hkv);
     dim3 grid(p.splits, hkv, batch);
+    if (d == 128 && rt >= 2 && page % kVTile == 0) {
+        if (rt == 2) return launch_pdl(kv4_verify_kernel<2>, grid, dim3(kThreads), 0, st, 1, p);
+        return launch_pdl(kv4_verify_kernel<4>, grid, dim3(kThreads), 0, st, 1, p);
+    }
 #define LQ2_ATTN(DD, RR) return launch_pdl(kv4_attention_kernel<DD, RR>, grid, dim3(kThreads), 0, st, 1, p)
     if (d == 128) {
         if (rt == 1) LQ2_ATTN(128, 1); else if (rt == 2) LQ2_ATTN(128, 2); else LQ2_ATTN(128, 4);

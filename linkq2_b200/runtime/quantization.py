@@ -211,7 +211,8 @@ def build_random(cfg: ModelConfig, *, seed=0, group_size=128, device="cuda:0", m
 
 
 @torch.no_grad()
-def save_random_checkpoint(path, cfg: ModelConfig, *, seed: int = 0, group_size: int = 128) -> Path:
+def save_random_checkpoint(path, cfg: ModelConfig, *, seed: int = 0, group_size: int = 128,
+                           weight_std: float = 0.05) -> Path:
     """Write a small seeded RTN-W4 checkpoint in the reference's on-disk layout
     (``qslab/compression/checkpoint.py:33-63``): every tensor is drawn from one CPU
     generator, so the same ``(cfg, seed)`` gives the same files wherever it runs.  The LM
@@ -242,7 +243,7 @@ def save_random_checkpoint(path, cfg: ModelConfig, *, seed: int = 0, group_size:
         for nm in ("self_attn.q_norm", "self_attn.k_norm"):
             tensors[p + nm + ".weight"] = (1 + 0.1 * torch.randn(d, generator=g)).half()
         for nm, shape in shapes.items():
-            w = (torch.randn(*shape, generator=g) * 0.05).half()
+            w = (torch.randn(*shape, generator=g) * weight_std).half()
             values, scale = rtn_quantize_(w, group_size)
             tensors[p + nm + ".weight"] = values.contiguous()
             tensors[p + nm + ".weight.scale"] = scale.contiguous()

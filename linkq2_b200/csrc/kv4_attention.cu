@@ -134,7 +134,10 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
     const int m_lo = v_lo ? r_lo / rep : 0, m_hi = v_hi ? r_hi / rep : 0;
     const int lim_lo = v_lo ? min(len + m_lo, capacity) : 0;
     const int lim_hi = v_hi ? min(len + m_hi, capacity) : 0;
-    uint32_t qa[KWT][2][4];
+    // Q' = q * ks is exact in fp32 and is carried as a high and a low fp16 part (two MMAs per operand):
+    // rounded to one fp16 it would shift every score of a row by the same channel-wise error, which
+    // does not average out over the tokens.
+    uint32_t qa[KWT][2][4], ql[KWT][2][4];
     {
         const __half* q_lo = p.q + int64_t(seq * p.m + m_lo) * p.q_stride + (kvh * rep + (v_lo ? r_lo % rep : 0)) * D;
         const __half* q_hi = p.q + int64_t(seq * p.m + m_hi) * p.q_stride + (kvh * rep + (v_hi ? r_hi % rep : 0)) * D;
@@ -142,12 +145,16 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
 #pragma unroll
         for (int wi = 0; wi < KWT; ++wi) {
             const int d0 = 8 * (t * KWT + wi);
-            float sc[8], lo[8], hi[8];
+            float lo[8], hi[8], lo2[8], hi2[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                sc[i] = __half2float(ksp[d0 + i]);
-                lo[i] = v_lo ? __half2float(q_lo[d0 + i]) * sc[i] : 0.f;
-                hi[i] = v_hi ? __half2float(q_hi[d0 + i]) * sc[i] : 0.f;
+                const float sc = __half2float(ksp[d0 + i]);
+                const float a = v_lo ? __half2float(q_lo[d0 + i]) * sc : 0.f;
+                const float b = v_hi ? __half2float(q_hi[d0 + i]) * sc : 0.f;
+                lo[i] = __half2float(__float2half_rn(a));
+                hi[i] = __half2float(__float2half_rn(b));
+                lo2[i] = a - lo[i];
+                hi2[i] = b - hi[i];
             }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -155,6 +162,10 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
                 qa[wi][h][1] = pack_h2(hi[2 * h], hi[2 * h + 4]);
                 qa[wi][h][2] = pack_h2(lo[2 * h + 1], lo[2 * h + 5]);
                 qa[wi][h][3] = pack_h2(hi[2 * h + 1], hi[2 * h + 5]);
+                ql[wi][h][0] = pack_h2(lo2[2 * h], lo2[2 * h + 4]);
+                ql[wi][h][1] = pack_h2(hi2[2 * h], hi2[2 * h + 4]);
+                ql[wi][h][2] = pack_h2(lo2[2 * h + 1], lo2[2 * h + 5]);
+                ql[wi][h][3] = pack_h2(hi2[2 * h + 1], hi2[2 * h + 5]);
             }
         }
     }
@@ -202,11 +213,11 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
         if (next < tile_end) fetch(next, kwn, vwn, vscn, live_n);
         if (live) {
             // ---- S = Q' K^T for 16 tokens (two n8 blocks)
-            float s[2][4];
+            float s[2][4], sl[2][4];
 #pragma unroll
             for (int n8 = 0; n8 < 2; ++n8) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) s[n8][c] = 0.f;
+                for (int c = 0; c < 4; ++c) s[n8][c] = sl[n8][c] = 0.f;
 #pragma unroll
                 for (int wi = 0; wi < KWT; ++wi) {
                     const uint32_t w = word_of(kw[n8], wi);
@@ -216,6 +227,7 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
                         const uint32_t b0 = h2_as_u32(__hsub2(u32_as_h2(and_or(x, 0x000f000fu, 0x64006400u)), k1032));
                         const uint32_t b1 = h2_as_u32(__hfma2(u32_as_h2(and_or(x, 0x00f000f0u, 0x64006400u)), k16th, km72));
                         mma_m16n8k16(s[n8], qa[wi][h][0], qa[wi][h][1], qa[wi][h][2], qa[wi][h][3], b0, b1);
+                        mma_m16n8k16(sl[n8], ql[wi][h][0], ql[wi][h][1], ql[wi][h][2], ql[wi][h][3], b0, b1);
                     }
                 }
             }
@@ -228,7 +240,7 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
                 for (int c = 0; c < 4; ++c) {
                     const int pos = pos0 + 8 * n8 + 2 * t + (c & 1);
                     const int lim = c < 2 ? lim_lo : lim_hi;
-                    const float v = pos < lim ? s[n8][c] * p.sl2 : -INFINITY;
+                    const float v = pos < lim ? (s[n8][c] + sl[n8][c]) * p.sl2 : -INFINITY;
                     s[n8][c] = v;
                     if (c < 2) t_lo = fmaxf(t_lo, v); else t_hi = fmaxf(t_hi, v);
                 }
@@ -373,16 +385,27 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
 // Replaces kv4_grouped_verify_kernel (qslab/kernels/kv4/grouped_attention.py:7-63), which
 // dequantises every K/V tile once per 16-row query block.  Here the CTA of one (sequence, KV
 // head, split) dequantises each 32-token tile ONCE, cooperatively, into shared memory as
-// fp16 - K as the exact integers (nibble - 8), the static K scale being folded into Q'; V as
-// fp16((nibble - 8) * vs), the rounding of the reference's kernel (:50-53) - and every warp
-// (one 16-row query tile each) reads its MMA operands from there with ldmatrix.  The packed
-// words of the next tile are in flight (registers) while the current one is multiplied, and
-// the two shared-memory buffers alternate, so there is one CTA barrier per tile.
-// Within every 8 channels the tile keeps the order the nibble masks produce, (0,4,1,5,2,6,3,7);
-// Q' is loaded in the same order and O is put back in natural order at the write-out.
+// the exact fp16 integers (nibble - 8), and every warp (one 16-row query tile each) reads its
+// MMA operands from there with ldmatrix.  The V scales (per token and group) multiply the
+// probabilities instead, P' = p * vs, so the codes stay exact.
+// The static K scale is folded into the queries, Q' = q * ks, which is exact in fp32 and is
+// kept in shared memory as a high and a low fp16 part (S = Q'hi K^T + Q'lo K^T): rounded to one
+// fp16 it would shift every score of a row by the same channel-wise error, and rounding
+// K * ks instead costs as much.
+// The packed words of the next two tiles are in flight (two register sets) while the current
+// tile is multiplied; the two fp16 buffers alternate, so there is one CTA barrier per tile.
+// Within every 8 channels the tiles keep the order the nibble masks produce, (0,4,1,5,2,6,3,7);
+// Q' is stored in the same order and O is put back in natural order at the write-out.
 // =====================================================================================
 constexpr int kVTile = 32;                 // tokens per tile
-constexpr int kVStride = 128 + 8;          // halves per token row: +16 bytes keep ldmatrix conflict-free
+constexpr int kVStride = 128 + 8;          // halves per row: +16 bytes keep ldmatrix conflict-free
+constexpr int kVTileHalves = kVTile * kVStride;
+
+template <int RT>
+struct VerifyLayout {
+    static constexpr int Q_HALVES = 16 * RT * kVStride;                 // one of the two parts of Q'
+    static constexpr int SMEM_BYTES = (2 * Q_HALVES + 4 * kVTileHalves) * 2;
+};
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem_row) {
     const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
@@ -399,9 +422,13 @@ template <int RT>
 __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParams p) {
     pdl_launch_dependents();
     pdl_wait();
-    constexpr int D = 128, NW = 16;
-    __shared__ __align__(16) __half sm_k[2][kVTile * kVStride];
-    __shared__ __align__(16) __half sm_v[2][kVTile * kVStride];
+    constexpr int D = 128, NW = 16, ROWS = 16 * RT;
+    extern __shared__ __align__(16) unsigned char vsm[];
+    __half* sm_qh = reinterpret_cast<__half*>(vsm);
+    __half* sm_ql = sm_qh + VerifyLayout<RT>::Q_HALVES;
+    __half* sm_k = sm_ql + VerifyLayout<RT>::Q_HALVES;      // [2][kVTileHalves]
+    __half* sm_v = sm_k + 2 * kVTileHalves;                 // [2][kVTileHalves]
+    __shared__ uint32_t sm_vs[2][kVTile];                   // V scales of the tile: (group 0, group 1) per token
     __shared__ int s_ticket;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -418,30 +445,57 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     const int tile_begin = split * per_split;
     const int tile_end = min(tiles, tile_begin + per_split);
 
-    // ---- Q' fragments of this warp's row tile (A operand, 8 k-chunks of 16 channels, stored order)
+    const int splits = p.splits;
+    float* part = p.partial + (int64_t(seq * p.hkv + kvh) * splits) * rows_valid * (D + 2);
+    const bool idle = tile_begin >= tile_end;               // block-uniform: a split beyond this sequence's end
+    if (idle && splits > 1) {                               // only its (max, denominator) = (-inf, 0) is recorded
+        for (int row = tid; row < rows_valid; row += kThreads) {
+            float* dst = part + (int64_t(split) * rows_valid + row) * (D + 2);
+            __stcg(dst + D, -INFINITY);
+            __stcg(dst + D + 1, 0.f);
+        }
+    }
+
+    // ---- Q' = q * ks of all rows, high and low parts, stored order
+    if (!idle) {
+        const __half* ksp = p.ks + kvh * D;
+        for (int idx = tid; idx < ROWS * NW; idx += kThreads) {
+            const int row = idx / NW, c8 = idx % NW;
+            __half hi[8], lo[8];
+            if (row < rows_valid) {
+                const __half* qp = p.q + int64_t(seq * p.m + row / rep) * p.q_stride + (kvh * rep + row % rep) * D + 8 * c8;
+                __half qraw[8], sraw[8];
+                *reinterpret_cast<uint4*>(sraw) = *reinterpret_cast<const uint4*>(ksp + 8 * c8);
+                if ((reinterpret_cast<uintptr_t>(qp) & 15) == 0) {
+                    *reinterpret_cast<uint4*>(qraw) = *reinterpret_cast<const uint4*>(qp);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) qraw[i] = qp[i];
+                }
+#pragma unroll
+                for (int ps = 0; ps < 8; ++ps) {             // stored position ps holds natural channel ps/2 + 4 (ps%2)
+                    const int i = (ps >> 1) + 4 * (ps & 1);
+                    const float v = __half2float(qraw[i]) * __half2float(sraw[i]);      // exact in fp32
+                    hi[ps] = __float2half_rn(v);
+                    lo[ps] = __float2half_rn(v - __half2float(hi[ps]));
+                }
+            } else {
+#pragma unroll
+                for (int ps = 0; ps < 8; ++ps) hi[ps] = lo[ps] = __float2half_rn(0.f);
+            }
+            *reinterpret_cast<uint4*>(sm_qh + row * kVStride + 8 * c8) = *reinterpret_cast<const uint4*>(hi);
+            *reinterpret_cast<uint4*>(sm_ql + row * kVStride + 8 * c8) = *reinterpret_cast<const uint4*>(lo);
+        }
+    }
+
     const bool mma_warp = warp < RT;
     const int r_lo = 16 * warp + g, r_hi = r_lo + 8;
     const bool v_lo = mma_warp && r_lo < rows_valid, v_hi = mma_warp && r_hi < rows_valid;
-    const int m_lo = v_lo ? r_lo / rep : 0, m_hi = v_hi ? r_hi / rep : 0;
-    const int lim_lo = v_lo ? min(len + m_lo, capacity) : 0;
-    const int lim_hi = v_hi ? min(len + m_hi, capacity) : 0;
-    uint32_t qa[8][4];
-    {
-        const __half* q_lo = p.q + int64_t(seq * p.m + m_lo) * p.q_stride + (kvh * rep + (v_lo ? r_lo % rep : 0)) * D;
-        const __half* q_hi = p.q + int64_t(seq * p.m + m_hi) * p.q_stride + (kvh * rep + (v_hi ? r_hi % rep : 0)) * D;
-        const __half* ksp = p.ks + kvh * D;
+    const int lim_lo = v_lo ? min(len + r_lo / rep, capacity) : 0;
+    const int lim_hi = v_hi ? min(len + r_hi / rep, capacity) : 0;
+    int lim_min = min(lim_lo, lim_hi);                        // tiles wholly below it need no mask
 #pragma unroll
-        for (int kc = 0; kc < 8; ++kc) {
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                // stored positions 2t, 2t+1 of an 8-channel chunk are the natural channels t and t + 4
-                const int d0 = 16 * kc + 8 * hf + t, d1 = d0 + 4;
-                const float s0 = __half2float(ksp[d0]), s1 = __half2float(ksp[d1]);
-                qa[kc][2 * hf] = pack_h2(v_lo ? __half2float(q_lo[d0]) * s0 : 0.f, v_lo ? __half2float(q_lo[d1]) * s1 : 0.f);
-                qa[kc][2 * hf + 1] = pack_h2(v_hi ? __half2float(q_hi[d0]) * s0 : 0.f, v_hi ? __half2float(q_hi[d1]) * s1 : 0.f);
-            }
-        }
-    }
+    for (int off = 1; off < 32; off <<= 1) lim_min = min(lim_min, __shfl_xor_sync(0xffffffffu, lim_min, off));
 
     float o[16][4];
 #pragma unroll
@@ -450,32 +504,44 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
         for (int c = 0; c < 4; ++c) o[j][c] = 0.f;
     float mx_lo = -INFINITY, mx_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
 
+    // lane-constant operand addresses
+    const __half* a_hi = sm_qh + (16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1)) * kVStride + 8 * (lane >> 4);
+    const __half* a_lo = a_hi + VerifyLayout<RT>::Q_HALVES;
+    const int kb_off = (lane & 7) * kVStride + (lane >> 3) * 8;
+    const int vb_off = (8 * ((lane >> 3) & 1) + (lane & 7)) * kVStride + (lane >> 4) * 8;
+
     // ---- cooperative dequantisation: thread (token = tid / 4, quarter = tid % 4) owns 4 K and 4 V words
     const int dq_tok = tid >> 2, dq_q = tid & 3;
+    const int dq_off = dq_tok * kVStride + 32 * dq_q;
     const __half2 k1032 = __floats2half2_rn(1032.f, 1032.f);
     const __half2 k16th = __floats2half2_rn(0.0625f, 0.0625f);
     const __half2 km72 = __floats2half2_rn(-72.f, -72.f);
-    const int vgrp = (32 * dq_q) >> p.vg_shift;
-    uint4 kw, vw;
-    __half vsc = __float2half_rn(0.f);
-    bool live = false;
+    const int64_t row_words = int64_t(p.hkv) * NW;
+    const int64_t lane_words = dq_tok * row_words + kvh * NW + 4 * dq_q;
+    uint4 kw[2], vw[2];
+    uint32_t vsc[2] = {0u, 0u};
+    bool live[2] = {false, false};
 
-    auto fetch = [&](int tile) {
+    auto fetch = [&](int tile, uint4& kw_, uint4& vw_, uint32_t& vsc_, bool& live_) {
+        live_ = false;
+        if (tile >= tile_end) return;
         const int pos0 = tile * kVTile;
         const int raw = p.bt[int64_t(seq) * p.max_blocks + pos0 / p.page];
-        live = raw >= 0;                                          // a tile never straddles pages (page % 32 == 0)
-        if (!live) return;
-        const int blk = min(raw, p.num_blocks - 1);
-        const int64_t slot = int64_t(blk) * p.page + pos0 % p.page + dq_tok;
-        kw = ldg_stream_u4(p.kq + (slot * p.hkv + kvh) * NW + 4 * dq_q);
-        vw = ldg_stream_u4(p.vq + (slot * p.hkv + kvh) * NW + 4 * dq_q);
-        vsc = p.vs[(slot * p.hkv + kvh) * p.ng + vgrp];
+        live_ = raw >= 0;                                         // a tile never straddles pages (page % 32 == 0)
+        if (!live_) return;
+        const int64_t slot0 = int64_t(min(raw, p.num_blocks - 1)) * p.page + pos0 % p.page;
+        kw_ = ldg_stream_u4(p.kq + slot0 * row_words + lane_words);
+        vw_ = ldg_stream_u4(p.vq + slot0 * row_words + lane_words);
+        if (dq_q == 0) {                                          // one lane per token fetches its scales
+            const __half* sp = p.vs + ((slot0 + dq_tok) * p.hkv + kvh) * p.ng;
+            vsc_ = p.ng == 2 ? *reinterpret_cast<const uint32_t*>(sp) : h2_as_u32(__half2half2(sp[0]));
+        }
     };
-    auto convert = [&](int buf) {                                 // registers -> fp16 rows of buffer `buf`
-        const uint32_t kws[4] = {kw.x, kw.y, kw.z, kw.w}, vws[4] = {vw.x, vw.y, vw.z, vw.w};
-        const __half2 sc2 = __half2half2(vsc);
-        __half* kdst = sm_k[buf] + dq_tok * kVStride + 32 * dq_q;
-        __half* vdst = sm_v[buf] + dq_tok * kVStride + 32 * dq_q;
+    auto convert = [&](int buf, const uint4& kw_, const uint4& vw_, uint32_t vsc_) {   // registers -> fp16 rows
+        const uint32_t kws[4] = {kw_.x, kw_.y, kw_.z, kw_.w}, vws[4] = {vw_.x, vw_.y, vw_.z, vw_.w};
+        if (dq_q == 0) sm_vs[buf][dq_tok] = vsc_;
+        __half* kdst = sm_k + buf * kVTileHalves + dq_off;
+        __half* vdst = sm_v + buf * kVTileHalves + dq_off;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const uint32_t a = kws[i], a8 = a >> 8, b = vws[i], b8 = b >> 8;
@@ -485,54 +551,60 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
             ko.y = h2_as_u32(__hfma2(u32_as_h2(and_or(a, 0x00f000f0u, 0x64006400u)), k16th, km72));
             ko.z = h2_as_u32(__hsub2(u32_as_h2(and_or(a8, 0x000f000fu, 0x64006400u)), k1032));
             ko.w = h2_as_u32(__hfma2(u32_as_h2(and_or(a8, 0x00f000f0u, 0x64006400u)), k16th, km72));
-            vo.x = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(b, 0x000f000fu, 0x64006400u)), k1032), sc2));
-            vo.y = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(b, 0x00f000f0u, 0x64006400u)), k16th, km72), sc2));
-            vo.z = h2_as_u32(__hmul2(__hsub2(u32_as_h2(and_or(b8, 0x000f000fu, 0x64006400u)), k1032), sc2));
-            vo.w = h2_as_u32(__hmul2(__hfma2(u32_as_h2(and_or(b8, 0x00f000f0u, 0x64006400u)), k16th, km72), sc2));
+            vo.x = h2_as_u32(__hsub2(u32_as_h2(and_or(b, 0x000f000fu, 0x64006400u)), k1032));
+            vo.y = h2_as_u32(__hfma2(u32_as_h2(and_or(b, 0x00f000f0u, 0x64006400u)), k16th, km72));
+            vo.z = h2_as_u32(__hsub2(u32_as_h2(and_or(b8, 0x000f000fu, 0x64006400u)), k1032));
+            vo.w = h2_as_u32(__hfma2(u32_as_h2(and_or(b8, 0x00f000f0u, 0x64006400u)), k16th, km72));
             *reinterpret_cast<uint4*>(kdst + 8 * i) = ko;
             *reinterpret_cast<uint4*>(vdst + 8 * i) = vo;
         }
     };
 
-    bool cur_live = false;
-    if (tile_begin < tile_end) {
-        fetch(tile_begin);
-        cur_live = live;
-        if (live) convert(0);
-    }
-    __syncthreads();
-    for (int tile = tile_begin; tile < tile_end; ++tile) {
-        const int buf = (tile - tile_begin) & 1;
-        const bool has_next = tile + 1 < tile_end;
-        if (has_next) fetch(tile + 1);                            // in flight during the MMAs below
-        const bool next_live = has_next && live;
+    // One tile: `par` is the parity of (tile - tile_begin): the fp16 buffer it reads and the register set
+    // the tile after next is fetched into.
+    auto step = [&](auto PAR, int tile) {
+        constexpr int par = decltype(PAR)::value;
+        const bool cur_live = live[par];
+        fetch(tile + 2, kw[par], vw[par], vsc[par], live[par]);  // this set was converted one step ago
         if (cur_live && mma_warp) {
-            const __half* kb = sm_k[buf];
-            const __half* vb = sm_v[buf];
-            // ---- S = Q' K^T: 16 rows x 32 tokens
-            float s[4][4];
+            const __half* kb = sm_k + par * kVTileHalves + kb_off;
+            const __half* vb = sm_v + par * kVTileHalves + vb_off;
+            // ---- S = Q' K^T: 16 rows x 32 tokens, high and low parts in separate accumulators
+            float s[4][4], sl[4][4];
 #pragma unroll
-            for (int n8 = 0; n8 < 4; ++n8) {
+            for (int n8 = 0; n8 < 4; ++n8)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) s[n8][c] = 0.f;
+                for (int c = 0; c < 4; ++c) s[n8][c] = sl[n8][c] = 0.f;
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {                  // 32 channels: two k-chunks per ldmatrix
+            for (int q4 = 0; q4 < 4; ++q4) {                      // 32 channels = two k-chunks per step
+                uint32_t ah0[4], ah1[4], al0[4], al1[4];
+                ldsm_x4(ah0, a_hi + 32 * q4);
+                ldsm_x4(ah1, a_hi + 32 * q4 + 16);
+                ldsm_x4(al0, a_lo + 32 * q4);
+                ldsm_x4(al1, a_lo + 32 * q4 + 16);
+#pragma unroll
+                for (int n8 = 0; n8 < 4; ++n8) {
                     uint32_t bf[4];
-                    ldsm_x4(bf, kb + (8 * n8 + (lane & 7)) * kVStride + (4 * q4 + (lane >> 3)) * 8);
-                    mma_m16n8k16(s[n8], qa[2 * q4][0], qa[2 * q4][1], qa[2 * q4][2], qa[2 * q4][3], bf[0], bf[1]);
-                    mma_m16n8k16(s[n8], qa[2 * q4 + 1][0], qa[2 * q4 + 1][1], qa[2 * q4 + 1][2], qa[2 * q4 + 1][3], bf[2], bf[3]);
+                    ldsm_x4(bf, kb + 8 * n8 * kVStride + 32 * q4);
+                    mma_m16n8k16(s[n8], ah0[0], ah0[1], ah0[2], ah0[3], bf[0], bf[1]);
+                    mma_m16n8k16(sl[n8], al0[0], al0[1], al0[2], al0[3], bf[0], bf[1]);
+                    mma_m16n8k16(s[n8], ah1[0], ah1[1], ah1[2], ah1[3], bf[2], bf[3]);
+                    mma_m16n8k16(sl[n8], al1[0], al1[1], al1[2], al1[3], bf[2], bf[3]);
                 }
             }
-            // ---- mask, online softmax (base-2 domain)
+            // ---- mask (last tiles only), online softmax in the base-2 domain
             const int pos0 = tile * kVTile;
+            const bool masked = pos0 + kVTile > lim_min;          // warp-uniform
             float t_lo = -INFINITY, t_hi = -INFINITY;
 #pragma unroll
             for (int n8 = 0; n8 < 4; ++n8) {
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    const int pos = pos0 + 8 * n8 + 2 * t + (c & 1);
-                    const int lim = c < 2 ? lim_lo : lim_hi;
-                    const float v = pos < lim ? s[n8][c] * p.sl2 : -INFINITY;
+                    float v = s[n8][c] + sl[n8][c];
+                    if (masked) {
+                        const int pos = pos0 + 8 * n8 + 2 * t + (c & 1);
+                        if (pos >= (c < 2 ? lim_lo : lim_hi)) v = -INFINITY;
+                    }
                     s[n8][c] = v;
                     if (c < 2) t_lo = fmaxf(t_lo, v); else t_hi = fmaxf(t_hi, v);
                 }
@@ -541,10 +613,10 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
             t_lo = fmaxf(t_lo, __shfl_xor_sync(0xffffffffu, t_lo, 2));
             t_hi = fmaxf(t_hi, __shfl_xor_sync(0xffffffffu, t_hi, 1));
             t_hi = fmaxf(t_hi, __shfl_xor_sync(0xffffffffu, t_hi, 2));
-            const float n_lo = fmaxf(mx_lo, t_lo), n_hi = fmaxf(mx_hi, t_hi);
+            const float n_lo = fmaxf(mx_lo, t_lo * p.sl2), n_hi = fmaxf(mx_hi, t_hi * p.sl2);   // sl2 > 0
             const float safe_lo = n_lo == -INFINITY ? 0.f : n_lo;
             const float safe_hi = n_hi == -INFINITY ? 0.f : n_hi;
-            const float a_lo = ex2(mx_lo - safe_lo), a_hi = ex2(mx_hi - safe_hi);
+            const float f_lo = ex2(mx_lo - safe_lo), f_hi = ex2(mx_hi - safe_hi);
             mx_lo = n_lo;
             mx_hi = n_hi;
             float sum_lo = 0.f, sum_hi = 0.f;
@@ -552,37 +624,61 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
             for (int n8 = 0; n8 < 4; ++n8) {
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    const float e = ex2(s[n8][c] - (c < 2 ? safe_lo : safe_hi));
+                    const float e = ex2(fmaf(s[n8][c], p.sl2, c < 2 ? -safe_lo : -safe_hi));
                     s[n8][c] = e;
                     if (c < 2) sum_lo += e; else sum_hi += e;
                 }
             }
-            l_lo = l_lo * a_lo + sum_lo;
-            l_hi = l_hi * a_hi + sum_hi;
-            if (__any_sync(0xffffffffu, a_lo != 1.f || a_hi != 1.f)) {
+            l_lo = l_lo * f_lo + sum_lo;
+            l_hi = l_hi * f_hi + sum_hi;
+            if (__any_sync(0xffffffffu, f_lo != 1.f || f_hi != 1.f)) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    o[j][0] *= a_lo; o[j][1] *= a_lo;
-                    o[j][2] *= a_hi; o[j][3] *= a_hi;
+                    o[j][0] *= f_lo; o[j][1] *= f_lo;
+                    o[j][2] *= f_hi; o[j][3] *= f_hi;
                 }
             }
-            // ---- O += P V: two k-chunks of 16 tokens, 16 blocks of 8 channels
+            // ---- O += P' V with P' = p * vs: two k-chunks of 16 tokens, 16 blocks of 8 channels, the first
+            // eight of group 0 and the last eight of group 1
 #pragma unroll
             for (int c16 = 0; c16 < 2; ++c16) {
-                const uint32_t pa0 = pack_h2(s[2 * c16][0], s[2 * c16][1]), pa1 = pack_h2(s[2 * c16][2], s[2 * c16][3]);
-                const uint32_t pa2 = pack_h2(s[2 * c16 + 1][0], s[2 * c16 + 1][1]), pa3 = pack_h2(s[2 * c16 + 1][2], s[2 * c16 + 1][3]);
+                // scales of tokens 8 n8 + 2t and + 1 for n8 = 2 c16 (x) and 2 c16 + 1 (y)
+                const uint2 va = *reinterpret_cast<const uint2*>(&sm_vs[par][16 * c16 + 2 * t]);
+                const uint2 vc = *reinterpret_cast<const uint2*>(&sm_vs[par][16 * c16 + 8 + 2 * t]);
+                uint32_t pa[2][4];
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const float a0 = __half2float(__ushort_as_half((unsigned short)(q ? va.x >> 16 : va.x & 0xffff)));
+                    const float a1 = __half2float(__ushort_as_half((unsigned short)(q ? va.y >> 16 : va.y & 0xffff)));
+                    const float c0 = __half2float(__ushort_as_half((unsigned short)(q ? vc.x >> 16 : vc.x & 0xffff)));
+                    const float c1 = __half2float(__ushort_as_half((unsigned short)(q ? vc.y >> 16 : vc.y & 0xffff)));
+                    pa[q][0] = pack_h2(s[2 * c16][0] * a0, s[2 * c16][1] * a1);
+                    pa[q][1] = pack_h2(s[2 * c16][2] * a0, s[2 * c16][3] * a1);
+                    pa[q][2] = pack_h2(s[2 * c16 + 1][0] * c0, s[2 * c16 + 1][1] * c1);
+                    pa[q][3] = pack_h2(s[2 * c16 + 1][2] * c0, s[2 * c16 + 1][3] * c1);
+                }
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) {                  // two channel blocks per ldmatrix
+                    constexpr int kHalf = 4;
+                    const int q = jj / kHalf;
                     uint32_t bf[4];
-                    ldsm_x4_trans(bf, vb + (16 * c16 + 8 * ((lane >> 3) & 1) + (lane & 7)) * kVStride + (2 * jj + (lane >> 4)) * 8);
-                    mma_m16n8k16(o[2 * jj], pa0, pa1, pa2, pa3, bf[0], bf[1]);
-                    mma_m16n8k16(o[2 * jj + 1], pa0, pa1, pa2, pa3, bf[2], bf[3]);
+                    ldsm_x4_trans(bf, vb + 16 * c16 * kVStride + 16 * jj);
+                    mma_m16n8k16(o[2 * jj], pa[q][0], pa[q][1], pa[q][2], pa[q][3], bf[0], bf[1]);
+                    mma_m16n8k16(o[2 * jj + 1], pa[q][0], pa[q][1], pa[q][2], pa[q][3], bf[2], bf[3]);
                 }
             }
         }
-        if (next_live) convert(buf ^ 1);
-        cur_live = next_live;
+        if (live[par ^ 1]) convert(par ^ 1, kw[par ^ 1], vw[par ^ 1], vsc[par ^ 1]);   // the next tile
         __syncthreads();
+    };
+
+    fetch(tile_begin, kw[0], vw[0], vsc[0], live[0]);
+    fetch(tile_begin + 1, kw[1], vw[1], vsc[1], live[1]);
+    if (live[0]) convert(0, kw[0], vw[0], vsc[0]);
+    __syncthreads();                                              // Q' and the first tile are in place
+    for (int tile = tile_begin; tile < tile_end; tile += 2) {
+        step(std::integral_constant<int, 0>{}, tile);
+        if (tile + 1 < tile_end) step(std::integral_constant<int, 1>{}, tile + 1);
     }
 
     // ---- write-out.  o[j][0..1] is (row r_lo, stored columns 8j + 2t, 8j + 2t + 1) = natural channels
@@ -591,9 +687,7 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-    const int splits = p.splits;
-    float* part = p.partial + (int64_t(seq * p.hkv + kvh) * splits) * rows_valid * (D + 2);
-    if (mma_warp) {
+    if (mma_warp && !(idle && splits > 1)) {
 #pragma unroll
         for (int hfr = 0; hfr < 2; ++hfr) {
             const int row = hfr ? r_hi : r_lo;
@@ -627,21 +721,27 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     __syncthreads();
     if (s_ticket != splits - 1) return;
     __threadfence();
-    for (int e = tid; e < rows_valid * D; e += kThreads) {
-        const int row = e / D, d = e % D;
+    for (int e = tid; e < rows_valid * (D / 2); e += kThreads) {
+        const int row = e / (D / 2), d = (e % (D / 2)) * 2;           // rows of D + 2 floats are 8-byte aligned
         float mx = -INFINITY;
         for (int sp = 0; sp < splits; ++sp)
             mx = fmaxf(mx, __ldcg(part + (int64_t(sp) * rows_valid + row) * (D + 2) + D));
         const float safe = mx == -INFINITY ? 0.f : mx;
-        float acc = 0.f, den = 0.f;
+        float acc0 = 0.f, acc1 = 0.f, den = 0.f;
         for (int sp = 0; sp < splits; ++sp) {
             const float* src = part + (int64_t(sp) * rows_valid + row) * (D + 2);
-            const float f = ex2(__ldcg(src + D) - safe);
-            acc += __ldcg(src + d) * f;
+            const float m_sp = __ldcg(src + D);
+            if (m_sp == -INFINITY) continue;                          // an idle split wrote no sums
+            const float f = ex2(m_sp - safe);
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(src + d));
+            acc0 += v.x * f;
+            acc1 += v.y * f;
             den += __ldcg(src + D + 1) * f;
         }
         const int mrow = row / rep, head = kvh * rep + row % rep;
-        p.out[(int64_t(seq * p.m + mrow) * p.hq + head) * D + d] = __float2half_rn(acc / fmaxf(den, 1e-20f));
+        const float inv = 1.f / fmaxf(den, 1e-20f);
+        *reinterpret_cast<__half2*>(p.out + (int64_t(seq * p.m + mrow) * p.hq + head) * D + d) =
+            __floats2half2_rn(acc0 * inv, acc1 * inv);
     }
     if (tid == 0) *counter = 0;
 }
@@ -696,7 +796,11 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
 }
 
 
-template <int D, int NG>
+// PAIR (at most four query rows): the eight MMA columns hold, for row r, the high part of the fp16-split
+// operand in column 2r and the low part in column 2r + 1, so lane t owns row t alone and both parts of a
+// product come out of the same MMA.  Otherwise column n is row n, lane t owns rows 2t and 2t + 1, the low
+// part of Q' takes a second MMA and P' stays one fp16.
+template <int D, int NG, bool PAIR>
 __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const AttnParams p, const int hpc) {
     pdl_launch_dependents();
     pdl_wait();
@@ -704,8 +808,9 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
     constexpr int NW = D / 8;             // words per (token, head)
     constexpr int KWT = NW / 4;           // K words per lane per token
     constexpr int VW = NW / 8;            // V words per lane per token (word wsel*8 + g)
-    constexpr int NO = 4 * VW;            // O accumulators per lane (each 16 dims x 8 rows)
+    constexpr int NO = 4 * VW;            // O accumulators per lane (each 16 dims x 8 columns)
     constexpr int KCH = D / 32;           // 16-byte chunks per lane per K (or V) tile
+    constexpr int NR = PAIR ? 1 : 2;      // query rows per lane
 
     extern __shared__ __align__(16) unsigned char fsm[];
     __shared__ int s_ticket;
@@ -728,13 +833,17 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
     const int first = tile_begin + ws;
     const int n_my = first < tile_end ? (tile_end - first + wt - 1) / wt : 0;
 
-    // ---- Q'^T fragments (B operand): column n = g is query row g; lane t covers words 4t..4t+3
-    const bool row_ok = g < rows_valid;
-    uint32_t qb[KWT][2][2];
+    // ---- Q'^T fragments (B operand), column n = g; lane t covers words 4t..4t+3.
+    // Q' = q * ks is exact in fp32 and is carried as a high and a low fp16 part: rounded to one fp16 it
+    // would shift every score of the row by the same channel-wise error, which does not average out over
+    // the tokens.
+    const int qrow = PAIR ? (g >> 1) : g;
+    const bool row_ok = qrow < rows_valid;
+    uint32_t qb[KWT][2][2], ql[PAIR ? 1 : KWT][2][2];
     float qsum = 0.f;
     {
-        const int mrow = row_ok ? g / rep : 0;
-        const __half* qp = p.q + int64_t(seq * p.m + mrow) * p.q_stride + (kvh * rep + (row_ok ? g % rep : 0)) * D;
+        const int mrow = row_ok ? qrow / rep : 0;
+        const __half* qp = p.q + int64_t(seq * p.m + mrow) * p.q_stride + (kvh * rep + (row_ok ? qrow % rep : 0)) * D;
         const __half* ksp = p.ks + kvh * D;
         const bool vec = (reinterpret_cast<uintptr_t>(qp) & 15) == 0;
 #pragma unroll
@@ -748,41 +857,63 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
 #pragma unroll
                 for (int i = 0; i < 8; ++i) qraw[i] = qp[d0 + i];
             }
-            __half qv[8];
+            __half qv[8], qw[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float v = row_ok ? __half2float(qraw[i]) * __half2float(sraw[i]) : 0.f;
+                const float v = row_ok ? __half2float(qraw[i]) * __half2float(sraw[i]) : 0.f;   // exact in fp32
+                float hi = __half2float(__float2half_rn(v));
+                float lo = __half2float(__float2half_rn(v - hi));
+                if (PAIR) { hi = (g & 1) ? lo : hi; lo = 0.f; }
                 // odd nibbles enter the A operand multiplied by 16
-                qv[i] = (i & 1) ? __float2half_rn(__half2float(__float2half_rn(v)) * 0.0625f) : __float2half_rn(v);
-                qsum += (i & 1) ? __half2float(qv[i]) * 16.f : __half2float(qv[i]);
+                qv[i] = __float2half_rn((i & 1) ? hi * 0.0625f : hi);
+                qw[i] = __float2half_rn((i & 1) ? lo * 0.0625f : lo);
+                qsum += ((i & 1) ? 16.f : 1.f) * (__half2float(qv[i]) + __half2float(qw[i]));
             }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 qb[wi][h][0] = h2_as_u32(__halves2half2(qv[2 * h], qv[2 * h + 4]));
                 qb[wi][h][1] = h2_as_u32(__halves2half2(qv[2 * h + 1], qv[2 * h + 5]));
+                if (!PAIR) {
+                    ql[wi][h][0] = h2_as_u32(__halves2half2(qw[2 * h], qw[2 * h + 4]));
+                    ql[wi][h][1] = h2_as_u32(__halves2half2(qw[2 * h + 1], qw[2 * h + 5]));
+                }
             }
         }
     }
     qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);                 // sum over all D for row g
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);                 // sum over all D for column g
     const float c1 = 16777216.f * p.sl2;
-    // this lane's accumulator columns are rows 2t and 2t+1
-    const float cq0 = 8.f * p.sl2 * __shfl_sync(0xffffffffu, qsum, (2 * t) * 4);
-    const float cq1 = 8.f * p.sl2 * __shfl_sync(0xffffffffu, qsum, (2 * t + 1) * 4);
-    const int r0 = 2 * t, r1 = 2 * t + 1;
-    const int lim0 = r0 < rows_valid ? min(len + r0 / rep, capacity) : 0;
-    const int lim1 = r1 < rows_valid ? min(len + r1 / rep, capacity) : 0;
-    const int lim_min = rows_valid == 8 ? min(len, capacity) : 0;   // a padded (invalid) row is masked everywhere
+    // rows of this lane: PAIR: row t (columns 2t, 2t+1 are its two parts); else rows 2t and 2t+1
+    const int rw[2] = {PAIR ? t : 2 * t, PAIR ? t : 2 * t + 1};
+    float cq[NR];
+    int lim[NR];
+    {
+        const float qa = __shfl_sync(0xffffffffu, qsum, (2 * t) * 4), qc = __shfl_sync(0xffffffffu, qsum, (2 * t + 1) * 4);
+        if (PAIR) {
+            cq[0] = 8.f * p.sl2 * (qa + qc);
+        } else {
+            cq[0] = 8.f * p.sl2 * qa;
+            cq[NR - 1] = 8.f * p.sl2 * qc;
+        }
+#pragma unroll
+        for (int r = 0; r < NR; ++r) lim[r] = rw[r] < rows_valid ? min(len + rw[r] / rep, capacity) : 0;
+    }
+    // a padded (invalid) row is masked everywhere
+    const int lim_min = rows_valid == (PAIR ? 4 : 8) ? min(len, capacity) : 0;
 
     float o[NO][4];
 #pragma unroll
     for (int j = 0; j < NO; ++j)
 #pragma unroll
         for (int c = 0; c < 4; ++c) o[j][c] = 0.f;
-    float mx0 = -INFINITY, mx1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float lp[NG][2];
+    float mx[NR], l[NR], lp[NG][NR];
 #pragma unroll
-    for (int q = 0; q < NG; ++q) lp[q][0] = lp[q][1] = 0.f;
+    for (int r = 0; r < NR; ++r) {
+        mx[r] = -INFINITY;
+        l[r] = 0.f;
+#pragma unroll
+        for (int q = 0; q < NG; ++q) lp[q][r] = 0.f;
+    }
 
     unsigned char* ring = fsm + warp * L::WARP_BYTES;
     const int64_t head_words = int64_t(p.hkv) * NW;
@@ -868,10 +999,11 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
             const unsigned char* kb = ring + slot * L::STAGE_BYTES;
             const unsigned char* vb = kb + L::K_BYTES;
             const int pos0 = (first + it * wt) * kFastTile;
-            float sv[2][4];
+            // sv[b16][2 * tok + r]: token 16 b16 + g + 8 tok, row rw[r]
+            float sv[2][2 * NR];
 #pragma unroll
             for (int b16 = 0; b16 < 2; ++b16) {
-                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                float acc[4] = {0.f, 0.f, 0.f, 0.f}, accl[4] = {0.f, 0.f, 0.f, 0.f};
                 const int tokA = 16 * b16 + g, tokB = tokA + 8;
                 uint32_t ka[KWT], kbw[KWT];
                 if (KWT == 4) {
@@ -891,37 +1023,54 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
                         const uint32_t wa = ka[wi] >> (8 * h), wb = kbw[wi] >> (8 * h);
                         mma_m16n8k16(acc, wa & 0x000f000fu, wb & 0x000f000fu, wa & 0x00f000f0u, wb & 0x00f000f0u,
                                      qb[wi][h][0], qb[wi][h][1]);
+                        if (!PAIR)
+                            mma_m16n8k16(accl, wa & 0x000f000fu, wb & 0x000f000fu, wa & 0x00f000f0u, wb & 0x00f000f0u,
+                                         ql[wi][h][0], ql[wi][h][1]);
                     }
                 }
-                sv[b16][0] = fmaf(acc[0], c1, -cq0);
-                sv[b16][1] = fmaf(acc[1], c1, -cq1);
-                sv[b16][2] = fmaf(acc[2], c1, -cq0);
-                sv[b16][3] = fmaf(acc[3], c1, -cq1);
+                if (PAIR) {
+                    sv[b16][0] = fmaf(acc[0] + acc[1], c1, -cq[0]);
+                    sv[b16][NR] = fmaf(acc[2] + acc[3], c1, -cq[0]);
+                } else {
+                    sv[b16][0] = fmaf(acc[0] + accl[0], c1, -cq[0]);
+                    sv[b16][NR - 1] = fmaf(acc[1] + accl[1], c1, -cq[NR - 1]);
+                    sv[b16][NR] = fmaf(acc[2] + accl[2], c1, -cq[0]);
+                    sv[b16][2 * NR - 1] = fmaf(acc[3] + accl[3], c1, -cq[NR - 1]);
+                }
                 if (pos0 + kFastTile > lim_min) {            // warp-uniform: only the last tiles need masks
                     const int pa = pos0 + tokA, pb = pos0 + tokB;
-                    if (pa >= lim0) sv[b16][0] = -INFINITY;
-                    if (pa >= lim1) sv[b16][1] = -INFINITY;
-                    if (pb >= lim0) sv[b16][2] = -INFINITY;
-                    if (pb >= lim1) sv[b16][3] = -INFINITY;
+#pragma unroll
+                    for (int r = 0; r < NR; ++r) {
+                        if (pa >= lim[r]) sv[b16][r] = -INFINITY;
+                        if (pb >= lim[r]) sv[b16][NR + r] = -INFINITY;
+                    }
                 }
             }
-            float t0 = fmaxf(fmaxf(sv[0][0], sv[0][2]), fmaxf(sv[1][0], sv[1][2]));
-            float t1 = fmaxf(fmaxf(sv[0][1], sv[0][3]), fmaxf(sv[1][1], sv[1][3]));
+            float tm[NR], safe[NR], al[NR];
+            bool moved = false;
 #pragma unroll
-            for (int off = 4; off < 32; off <<= 1) {
-                t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
-                t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+            for (int r = 0; r < NR; ++r) {
+                tm[r] = fmaxf(fmaxf(sv[0][r], sv[0][NR + r]), fmaxf(sv[1][r], sv[1][NR + r]));
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) tm[r] = fmaxf(tm[r], __shfl_xor_sync(0xffffffffu, tm[r], off));
+                const float n = fmaxf(mx[r], tm[r]);
+                safe[r] = n == -INFINITY ? 0.f : n;
+                al[r] = ex2(mx[r] - safe[r]);
+                mx[r] = n;
+                moved = moved || al[r] != 1.f;
             }
-            const float n0 = fmaxf(mx0, t0), n1 = fmaxf(mx1, t1);
-            const float safe0 = n0 == -INFINITY ? 0.f : n0, safe1 = n1 == -INFINITY ? 0.f : n1;
-            const float a0 = ex2(mx0 - safe0), a1 = ex2(mx1 - safe1);
-            mx0 = n0; mx1 = n1;
-            if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
-                l0 *= a0; l1 *= a1;
+            if (__any_sync(0xffffffffu, moved)) {
 #pragma unroll
-                for (int q = 0; q < NG; ++q) { lp[q][0] *= a0; lp[q][1] *= a1; }
+                for (int r = 0; r < NR; ++r) {
+                    l[r] *= al[r];
 #pragma unroll
-                for (int j = 0; j < NO; ++j) { o[j][0] *= a0; o[j][1] *= a1; o[j][2] *= a0; o[j][3] *= a1; }
+                    for (int q = 0; q < NG; ++q) lp[q][r] *= al[r];
+                }
+                // accumulator columns 2t, 2t+1: both belong to row t (PAIR) or to rows 2t, 2t+1
+#pragma unroll
+                for (int j = 0; j < NO; ++j) {
+                    o[j][0] *= al[0]; o[j][1] *= al[NR - 1]; o[j][2] *= al[0]; o[j][3] *= al[NR - 1];
+                }
             }
             // The codes enter the MMAs as unsigned values, so the raw sums are large and positive while the
             // result (after the -8 * sum P' term) is small.  The tensor core truncates when it adds into its
@@ -931,10 +1080,13 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
             float ot[NO][4];
 #pragma unroll
             for (int b16 = 0; b16 < 2; ++b16) {
-                const float p0 = ex2(sv[b16][0] - safe0), p1 = ex2(sv[b16][1] - safe1);
-                const float p2 = ex2(sv[b16][2] - safe0), p3 = ex2(sv[b16][3] - safe1);
-                l0 += p0 + p2;
-                l1 += p1 + p3;
+                float pr[2 * NR];
+#pragma unroll
+                for (int r = 0; r < NR; ++r) {
+                    pr[r] = ex2(sv[b16][r] - safe[r]);
+                    pr[NR + r] = ex2(sv[b16][NR + r] - safe[r]);
+                    l[r] += pr[r] + pr[NR + r];
+                }
                 const uint32_t sA = __shfl_sync(0xffffffffu, sc_cur, 16 * b16 + g);
                 const uint32_t sB = __shfl_sync(0xffffffffu, sc_cur, 16 * b16 + g + 8);
                 const unsigned char* vrow = vb + (16 * b16) * L::VROW;
@@ -942,12 +1094,24 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
                 for (int q = 0; q < NG; ++q) {
                     const float fa = __half2float(__ushort_as_half((unsigned short)(q ? (sA >> 16) : (sA & 0xffff))));
                     const float fb = __half2float(__ushort_as_half((unsigned short)(q ? (sB >> 16) : (sB & 0xffff))));
-                    // P' is rounded to fp16 for the MMA; the offset term -8 * sum P' must use the same
-                    // rounded values, or the rounding noise would enter the result multiplied by 8
-                    const uint32_t h01 = pack_h2(p0 * fa, p1 * fa), h23 = pack_h2(p2 * fb, p3 * fb);
-                    const float2 r01 = __half22float2(u32_as_h2(h01)), r23 = __half22float2(u32_as_h2(h23));
-                    lp[q][0] += r01.x + r23.x;
-                    lp[q][1] += r01.y + r23.y;
+                    // P' = p * vs enters the MMA as fp16: PAIR carries its rounding remainder in the odd column;
+                    // otherwise it is one fp16.  The offset term -8 * sum P' must be summed from the same
+                    // rounded values, or the rounding noise would enter the result multiplied by 8.
+                    uint32_t h01, h23;
+                    if (PAIR) {
+                        const float xa = pr[0] * fa, xb = pr[1] * fb;
+                        const __half ha = __float2half_rn(xa), hb = __float2half_rn(xb);
+                        const __half la = __float2half_rn(xa - __half2float(ha)), lb = __float2half_rn(xb - __half2float(hb));
+                        h01 = h2_as_u32(__halves2half2(ha, la));
+                        h23 = h2_as_u32(__halves2half2(hb, lb));
+                        lp[q][0] += (__half2float(ha) + __half2float(la)) + (__half2float(hb) + __half2float(lb));
+                    } else {
+                        h01 = pack_h2(pr[0] * fa, pr[NR - 1] * fa);
+                        h23 = pack_h2(pr[NR] * fb, pr[2 * NR - 1] * fb);
+                        const float2 r01 = __half22float2(u32_as_h2(h01)), r23 = __half22float2(u32_as_h2(h23));
+                        lp[q][0] += r01.x + r23.x;
+                        lp[q][NR - 1] += r01.y + r23.y;
+                    }
                     const uint32_t b0 = movmatrix_trans(h01);
                     const uint32_t b1 = movmatrix_trans(h23);
 #pragma unroll
@@ -981,32 +1145,41 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
     }
     cp_async_wait<0>();
 
-    // ---- per-warp results: rows 2t, 2t+1 of 16 * VW * ... dims; denominators summed over the 8 lane groups
+    // ---- per-warp results; denominators and offset sums are summed over the 8 lane groups
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
 #pragma unroll
-        for (int q = 0; q < NG; ++q) {
-            lp[q][0] += __shfl_xor_sync(0xffffffffu, lp[q][0], off);
-            lp[q][1] += __shfl_xor_sync(0xffffffffu, lp[q][1], off);
+        for (int r = 0; r < NR; ++r) {
+            l[r] += __shfl_xor_sync(0xffffffffu, l[r], off);
+#pragma unroll
+            for (int q = 0; q < NG; ++q) lp[q][r] += __shfl_xor_sync(0xffffffffu, lp[q][r], off);
         }
     }
     __syncthreads();                                   // all rings are idle: reuse them for the merge
     float* mo = reinterpret_cast<float*>(fsm) + warp * 8 * (D + 2);     // [8 rows][D + 2]
+    // accumulator element c of o[j]: dimension `dim` (c < 2, codes times 2^-24) or `dim + 1` (c >= 2, the odd
+    // nibble, codes times 2^-20); column 2t + (c & 1)
 #pragma unroll
     for (int j = 0; j < NO; ++j) {
         const int wsel = j / 4, b = j % 4;
         const int grp = NG == 2 ? wsel : 0;
         const int dim = 8 * (wsel * 8 + g) + 2 * b;
-        mo[r0 * (D + 2) + dim] = o[j][0] * 16777216.f - 8.f * lp[grp][0];
-        mo[r1 * (D + 2) + dim] = o[j][1] * 16777216.f - 8.f * lp[grp][1];
-        mo[r0 * (D + 2) + dim + 1] = o[j][2] * 1048576.f - 8.f * lp[grp][0];
-        mo[r1 * (D + 2) + dim + 1] = o[j][3] * 1048576.f - 8.f * lp[grp][1];
+        if (PAIR) {
+            mo[rw[0] * (D + 2) + dim] = (o[j][0] + o[j][1]) * 16777216.f - 8.f * lp[grp][0];
+            mo[rw[0] * (D + 2) + dim + 1] = (o[j][2] + o[j][3]) * 1048576.f - 8.f * lp[grp][0];
+        } else {
+            mo[rw[0] * (D + 2) + dim] = o[j][0] * 16777216.f - 8.f * lp[grp][0];
+            mo[rw[1] * (D + 2) + dim] = o[j][1] * 16777216.f - 8.f * lp[grp][NR - 1];
+            mo[rw[0] * (D + 2) + dim + 1] = o[j][2] * 1048576.f - 8.f * lp[grp][0];
+            mo[rw[1] * (D + 2) + dim + 1] = o[j][3] * 1048576.f - 8.f * lp[grp][NR - 1];
+        }
     }
     if (g == 0) {
-        mo[r0 * (D + 2) + D] = mx0; mo[r0 * (D + 2) + D + 1] = l0;
-        mo[r1 * (D + 2) + D] = mx1; mo[r1 * (D + 2) + D + 1] = l1;
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            mo[rw[r] * (D + 2) + D] = mx[r];
+            mo[rw[r] * (D + 2) + D + 1] = l[r];
+        }
     }
     __syncthreads();
 
@@ -1104,7 +1277,6 @@ int row_tiles(int m, int hq, int hkv) {
 }  // namespace
 
 int kv4_attention_splits(int batch, int m, int hq, int hkv, int d, int page, int max_blocks) {
-    (void)d;
     const int64_t capacity = int64_t(max_blocks) * page;
     // Shapes only.  Enough splits to fill one resident wave (two CTAs per SM), no warp longer
     // than 1024 tokens (so one long sequence in a batch cannot become the tail), never less
@@ -1120,7 +1292,14 @@ int kv4_attention_splits(int batch, int m, int hq, int hkv, int d, int page, int
     }
     const int base = batch * (hkv / hpc);
     int64_t splits = (fast ? 2 : 4) * kNumSMs / base;    // floor: the grid stays within one resident wave
-    const int64_t by_len = cdiv64(capacity, int64_t(1024) * wt);
+    int64_t by_len = cdiv64(capacity, int64_t(1024) * wt);
+    // The verify kernel (one CTA walks its tokens alone, three CTAs per SM) is compute-bound and its grid
+    // usually exceeds one wave: short CTAs (256 tokens) let the block scheduler level the SMs, so the last
+    // wave costs 8 tiles instead of a whole split.
+    if (!fast && d == 128 && row_tiles(m, hq, hkv) >= 2 && page % kVTile == 0) {
+        splits = cdiv64(3 * kNumSMs, base);
+        by_len = cdiv64(capacity, 256);
+    }
     if (by_len > splits) splits = by_len;
     const int64_t most = capacity / 256 > 0 ? capacity / 256 : 1;
     if (splits > most) splits = most;
@@ -1188,24 +1367,42 @@ int kv4_attention_launch(const __half* q, int64_t q_stride, const uint32_t* kq, 
         static bool configured[64] = {};
         int dev = 0;
         if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LQ2_ERR_CUDA;
+        const bool pair = m * (hq / hkv) <= 4;
+#define LQ2_FAST_ATTR(DD, GG, PP) \
+    (cudaFuncSetAttribute(kv4_decode_fast_kernel<DD, GG, PP>, cudaFuncAttributeMaxDynamicSharedMemorySize, FastLayout<DD>::SMEM_BYTES) == cudaSuccess)
+#define LQ2_FAST(DD, GG, PP) \
+    return launch_pdl(kv4_decode_fast_kernel<DD, GG, PP>, fgrid, dim3(kFastThreads), FastLayout<DD>::SMEM_BYTES, st, 1, p, hpc)
         if (!configured[dev]) {
-            bool ok = cudaFuncSetAttribute(kv4_decode_fast_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, FastLayout<128>::SMEM_BYTES) == cudaSuccess;
-            ok = ok && cudaFuncSetAttribute(kv4_decode_fast_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, FastLayout<128>::SMEM_BYTES) == cudaSuccess;
-            ok = ok && cudaFuncSetAttribute(kv4_decode_fast_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, FastLayout<64>::SMEM_BYTES) == cudaSuccess;
+            const bool ok = LQ2_FAST_ATTR(128, 1, true) && LQ2_FAST_ATTR(128, 2, true) && LQ2_FAST_ATTR(64, 1, true) &&
+                            LQ2_FAST_ATTR(128, 1, false) && LQ2_FAST_ATTR(128, 2, false) && LQ2_FAST_ATTR(64, 1, false);
             if (!ok) return LQ2_ERR_CUDA;
             configured[dev] = true;
         }
-        if (d == 128 && p.ng == 2)
-            return launch_pdl(kv4_decode_fast_kernel<128, 2>, fgrid, dim3(kFastThreads), FastLayout<128>::SMEM_BYTES, st, 1, p, hpc);
-        if (d == 128)
-            return launch_pdl(kv4_decode_fast_kernel<128, 1>, fgrid, dim3(kFastThreads), FastLayout<128>::SMEM_BYTES, st, 1, p, hpc);
-        return launch_pdl(kv4_decode_fast_kernel<64, 1>, fgrid, dim3(kFastThreads), FastLayout<64>::SMEM_BYTES, st, 1, p, hpc);
+        if (pair) {
+            if (d == 128 && p.ng == 2) LQ2_FAST(128, 2, true);
+            if (d == 128) LQ2_FAST(128, 1, true);
+            LQ2_FAST(64, 1, true);
+        }
+        if (d == 128 && p.ng == 2) LQ2_FAST(128, 2, false);
+        if (d == 128) LQ2_FAST(128, 1, false);
+        LQ2_FAST(64, 1, false);
+#undef LQ2_FAST
+#undef LQ2_FAST_ATTR
     }
     const int rt = row_tiles(m, hq, hkv);
     dim3 grid(p.splits, hkv, batch);
-    if (d == 128 && rt >= 2 && page % kVTile == 0) {
-        if (rt == 2) return launch_pdl(kv4_verify_kernel<2>, grid, dim3(kThreads), 0, st, 1, p);
-        return launch_pdl(kv4_verify_kernel<4>, grid, dim3(kThreads), 0, st, 1, p);
+    if (d == 128 && rt >= 2 && page % kVTile == 0 && p.ng <= 2) {
+        static bool verify_ready[64] = {};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LQ2_ERR_CUDA;
+        if (!verify_ready[dev]) {
+            if (cudaFuncSetAttribute(kv4_verify_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, VerifyLayout<2>::SMEM_BYTES) != cudaSuccess ||
+                cudaFuncSetAttribute(kv4_verify_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, VerifyLayout<4>::SMEM_BYTES) != cudaSuccess)
+                return LQ2_ERR_CUDA;
+            verify_ready[dev] = true;
+        }
+        if (rt == 2) return launch_pdl(kv4_verify_kernel<2>, grid, dim3(kThreads), VerifyLayout<2>::SMEM_BYTES, st, 1, p);
+        return launch_pdl(kv4_verify_kernel<4>, grid, dim3(kThreads), VerifyLayout<4>::SMEM_BYTES, st, 1, p);
     }
 #define LQ2_ATTN(DD, RR) return launch_pdl(kv4_attention_kernel<DD, RR>, grid, dim3(kThreads), 0, st, 1, p)
     if (d == 128) {

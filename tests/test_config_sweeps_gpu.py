@@ -10,6 +10,13 @@ and within max-abs-error / RMS <= 1e-2 of the oracle's unrounded fp32 outputs; t
 covered by a size-independent property (a second run returns identical bits, every
 output is finite and bounded by the largest dequantised value).
 
+The attention operators return fp16 (the reference's signature).  With the x10 outlier
+channels the largest outputs are ~30 x the RMS, so the final rounding to fp16 alone - half
+an fp16 ulp of the value - reaches 1.15e-2 RMS at 20 k tokens of context: an exactly
+computed result, rounded once, already misses a plain 1e-2 bound.  The attention bound is
+therefore |got - ref| <= 1e-2 RMS + ulp_fp16(ref) / 2 element by element: 1e-2 RMS for
+the arithmetic, plus the one rounding the output type imposes.
+
 W4A16 (configuration 2): the four projection shapes x M in {1, 4, 8, 16, 64, 256, 2048},
 symmetric and affine group-128 quantization, activations with 1 % outlier columns x20,
 max-abs-error / RMS <= 1e-2 against an fp32 matmul on the oracle's dequantised weight.
@@ -27,6 +34,19 @@ TOL = 1e-2
 
 def err_over_rms(actual, expected):
     return float((actual - expected).abs().max() / expected.pow(2).mean().sqrt().clamp_min(1e-12))
+
+
+def half_ulp_fp16(x):
+    """Half the spacing of fp16 numbers at |x| (subnormal spacing 2**-24 below 2**-14)."""
+    exponent = torch.floor(torch.log2(x.abs().clamp_min(2.0 ** -14)))
+    return torch.exp2(exponent - 11)
+
+
+def attention_err_over_rms(actual, expected):
+    """max(|actual - expected| - ulp_fp16(expected) / 2, 0) / RMS(expected), ``actual`` being fp16
+    values: the error of the arithmetic, without the final rounding of the fp16 output."""
+    excess = ((actual - expected).abs() - half_ulp_fp16(expected)).clamp_min(0)
+    return float(excess.max() / expected.pow(2).mean().sqrt().clamp_min(1e-12))
 
 
 def make_kv(tokens, hkv, seed, channels_k, channels_v):
@@ -132,7 +152,7 @@ def test_kv4_decode_and_verify_at_specified_sizes(batch, hkv):
         ref = ok.paged_attention_decode(q[rows], kc, vc, compact, ctx[ids], block_n=PAGE, num_kv_heads=hkv,
                                         v_group=VGROUP, verify_m=m, out_dtype=torch.float32)
         got = out[rows.cuda()].float().cpu()
-        assert err_over_rms(got, ref) <= TOL, (m, err_over_rms(got, ref))
+        assert attention_err_over_rms(got, ref) <= TOL, (m, attention_err_over_rms(got, ref), err_over_rms(got, ref))
 
 
 @pytest.mark.parametrize("batch", [96, 160])
@@ -147,7 +167,8 @@ def test_kv4_decode_many_short_sequences(batch):
                                  num_kv_heads=HKV, v_group=VGROUP)
     ref = ok.paged_attention_decode(q[ids], kc, vc, compact, lens[ids].int(), block_n=PAGE, num_kv_heads=HKV,
                                     v_group=VGROUP, out_dtype=torch.float32)
-    assert err_over_rms(out[torch.tensor(ids).cuda()].float().cpu(), ref) <= TOL
+    got = out[torch.tensor(ids).cuda()].float().cpu()
+    assert attention_err_over_rms(got, ref) <= TOL, (attention_err_over_rms(got, ref), err_over_rms(got, ref))
 
 
 # ---------------------------------------------------------------------------------- W4A16

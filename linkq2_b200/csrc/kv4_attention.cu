@@ -94,6 +94,62 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// A split's partial: per row D sums, then (running max in the base-2 domain, denominator), padded to
+// D + 4 floats so that rows are 16-byte aligned.
+__host__ __device__ constexpr int part_row(int d) { return d + 4; }
+
+// Merge of the split partials by the last CTA of a (sequence, head group).  `units` heads x `rows` rows;
+// part_of(u) is the base of unit u's [splits][rows][D + 4] partials.  The (max, denominator) pairs are
+// first brought to shared memory in one sweep - read on demand they would put two dependent memory round
+// trips per split on every thread's path - and the sums are then read four splits at a time with
+// independent 16-byte loads.  A split that saw no token wrote (-inf, 0) and possibly no sums: its sums are
+// never used.  sm_stat needs units * splits * rows entries.
+template <int D, int THREADS, typename PartOf, typename Store>
+__device__ __forceinline__ void merge_splits(int units, int rows, int splits, float2* sm_stat, PartOf part_of,
+                                             Store store) {
+    constexpr int RS = part_row(D), V = D / 4;
+    const int tid = threadIdx.x;
+    const int per_unit = splits * rows;
+    for (int i = tid; i < units * per_unit; i += THREADS) {
+        const int u = i / per_unit, r = i - u * per_unit;                 // r = split * rows + row
+        sm_stat[i] = __ldcg(reinterpret_cast<const float2*>(part_of(u) + int64_t(r) * RS + D));
+    }
+    __syncthreads();
+    for (int e = tid; e < units * rows * V; e += THREADS) {
+        const int d = (e % V) * 4, ur = e / V, u = ur / rows, row = ur - u * rows;
+        const float2* st = sm_stat + u * per_unit + row;
+        float mx = -INFINITY;
+        for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, st[sp * rows].x);
+        const float safe = mx == -INFINITY ? 0.f : mx;
+        const float* src = part_of(u) + int64_t(row) * RS + d;
+        const int64_t step = int64_t(rows) * RS;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        float den = 0.f;
+        auto add = [&](const float4& v, const float2& s2) {
+            if (s2.x != -INFINITY) {
+                const float f = ex2(s2.x - safe);
+                acc.x += v.x * f; acc.y += v.y * f; acc.z += v.z * f; acc.w += v.w * f;
+                den += s2.y * f;
+            }
+        };
+        int sp = 0;
+        for (; sp + 4 <= splits; sp += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = __ldcg(reinterpret_cast<const float4*>(src + (sp + k) * step));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) add(v[k], st[(sp + k) * rows]);
+        }
+        for (; sp < splits; ++sp) add(__ldcg(reinterpret_cast<const float4*>(src + sp * step)), st[sp * rows]);
+        store(u, row, d, acc, 1.f / fmaxf(den, 1e-20f));
+    }
+}
+
+__device__ __forceinline__ void store_h4(__half* dst, const float4& a, float inv) {
+    const __half2 h01 = __floats2half2_rn(a.x * inv, a.y * inv), h23 = __floats2half2_rn(a.z * inv, a.w * inv);
+    *reinterpret_cast<uint2*>(dst) = make_uint2(h2_as_u32(h01), h2_as_u32(h23));
+}
+
 // RT: 16-row query tiles per (sequence, KV head): ceil(M * rep / 16), 3 rounded up to 4.
 template <int D, int RT>
 __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParams p) {
@@ -108,7 +164,8 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
     using KW = typename KWords<D>::type;
     using VW = typename VWords<D>::type;
 
-    __shared__ float sm_o[kWarps][16][D];
+    __shared__ __align__(16) float sm_raw[kWarps * 16 * 128];       // 32 KB: per-warp sums, later the merge's pairs
+    float (*sm_o)[16][D] = reinterpret_cast<float (*)[16][D]>(sm_raw);
     __shared__ float sm_m[kWarps][16];
     __shared__ float sm_l[kWarps][16];
     __shared__ int s_ticket;
@@ -326,7 +383,7 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
 
     // ---- merge the WT warps of each row tile; write the result or this split's partial
     const int splits = p.splits;
-    float* part = p.partial + (int64_t(seq * p.hkv + kvh) * splits) * rows_valid * (D + 2);
+    float* part = p.partial + (int64_t(seq * p.hkv + kvh) * splits) * rows_valid * part_row(D);
     for (int e = tid; e < ROWS * D; e += kThreads) {
         const int row = e / D, d = e % D;
         if (row >= rows_valid) continue;
@@ -346,7 +403,7 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
             const int mrow = row / rep, head = kvh * rep + row % rep;
             p.out[(int64_t(seq * p.m + mrow) * p.hq + head) * D + d] = __float2half_rn(acc / fmaxf(den, 1e-20f));
         } else {
-            float* dst = part + (int64_t(split) * rows_valid + row) * (D + 2);
+            float* dst = part + (int64_t(split) * rows_valid + row) * part_row(D);
             __stcg(dst + d, acc);
             if (d == 0) { __stcg(dst + D, mx); __stcg(dst + D + 1, den); }
         }
@@ -360,22 +417,11 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
     __syncthreads();
     if (s_ticket != splits - 1) return;
     __threadfence();
-    for (int e = tid; e < rows_valid * D; e += kThreads) {
-        const int row = e / D, d = e % D;
-        float mx = -INFINITY;
-        for (int sp = 0; sp < splits; ++sp)
-            mx = fmaxf(mx, __ldcg(part + (int64_t(sp) * rows_valid + row) * (D + 2) + D));
-        const float safe = mx == -INFINITY ? 0.f : mx;
-        float acc = 0.f, den = 0.f;
-        for (int sp = 0; sp < splits; ++sp) {
-            const float* src = part + (int64_t(sp) * rows_valid + row) * (D + 2);
-            const float f = exp2f(__ldcg(src + D) - safe);
-            acc += __ldcg(src + d) * f;
-            den += __ldcg(src + D + 1) * f;
-        }
-        const int mrow = row / rep, head = kvh * rep + row % rep;
-        p.out[(int64_t(seq * p.m + mrow) * p.hq + head) * D + d] = __float2half_rn(acc / fmaxf(den, 1e-20f));
-    }
+    merge_splits<D, kThreads>(
+        1, rows_valid, splits, reinterpret_cast<float2*>(sm_raw), [&](int) { return part; },
+        [&](int, int row, int d, const float4& acc, float inv) {
+            store_h4(p.out + (int64_t(seq * p.m + row / rep) * p.hq + kvh * rep + row % rep) * D + d, acc, inv);
+        });
     if (tid == 0) *counter = 0;
 }
 
@@ -446,11 +492,11 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     const int tile_end = min(tiles, tile_begin + per_split);
 
     const int splits = p.splits;
-    float* part = p.partial + (int64_t(seq * p.hkv + kvh) * splits) * rows_valid * (D + 2);
+    float* part = p.partial + (int64_t(seq * p.hkv + kvh) * splits) * rows_valid * part_row(D);
     const bool idle = tile_begin >= tile_end;               // block-uniform: a split beyond this sequence's end
     if (idle && splits > 1) {                               // only its (max, denominator) = (-inf, 0) is recorded
         for (int row = tid; row < rows_valid; row += kThreads) {
-            float* dst = part + (int64_t(split) * rows_valid + row) * (D + 2);
+            float* dst = part + (int64_t(split) * rows_valid + row) * part_row(D);
             __stcg(dst + D, -INFINITY);
             __stcg(dst + D + 1, 0.f);
         }
@@ -521,14 +567,16 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     uint4 kw[2], vw[2];
     uint32_t vsc[2] = {0u, 0u};
     bool live[2] = {false, false};
+    int raw_ahead = -1;
 
-    auto fetch = [&](int tile, uint4& kw_, uint4& vw_, uint32_t& vsc_, bool& live_) {
-        live_ = false;
-        if (tile >= tile_end) return;
-        const int pos0 = tile * kVTile;
-        const int raw = p.bt[int64_t(seq) * p.max_blocks + pos0 / p.page];
-        live_ = raw >= 0;                                         // a tile never straddles pages (page % 32 == 0)
+    // The block-table entry of a tile decides whether the tile is fetched at all, so waiting for it would
+    // stall the warp for a memory round trip per tile: it is read one step before it is used.
+    const int32_t* bt_row = p.bt + int64_t(seq) * p.max_blocks;
+    auto table_entry = [&](int tile) { return tile < tile_end ? bt_row[tile * kVTile / p.page] : -1; };
+    auto fetch = [&](int tile, int raw, uint4& kw_, uint4& vw_, uint32_t& vsc_, bool& live_) {
+        live_ = tile < tile_end && raw >= 0;                      // a tile never straddles pages (page % 32 == 0)
         if (!live_) return;
+        const int pos0 = tile * kVTile;
         const int64_t slot0 = int64_t(min(raw, p.num_blocks - 1)) * p.page + pos0 % p.page;
         kw_ = ldg_stream_u4(p.kq + slot0 * row_words + lane_words);
         vw_ = ldg_stream_u4(p.vq + slot0 * row_words + lane_words);
@@ -565,7 +613,9 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     auto step = [&](auto PAR, int tile) {
         constexpr int par = decltype(PAR)::value;
         const bool cur_live = live[par];
-        fetch(tile + 2, kw[par], vw[par], vsc[par], live[par]);  // this set was converted one step ago
+        const int raw_now = raw_ahead;
+        raw_ahead = table_entry(tile + 3);
+        fetch(tile + 2, raw_now, kw[par], vw[par], vsc[par], live[par]);   // this set was converted one step ago
         if (cur_live && mma_warp) {
             const __half* kb = sm_k + par * kVTileHalves + kb_off;
             const __half* vb = sm_v + par * kVTileHalves + vb_off;
@@ -672,8 +722,9 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
         __syncthreads();
     };
 
-    fetch(tile_begin, kw[0], vw[0], vsc[0], live[0]);
-    fetch(tile_begin + 1, kw[1], vw[1], vsc[1], live[1]);
+    fetch(tile_begin, table_entry(tile_begin), kw[0], vw[0], vsc[0], live[0]);
+    fetch(tile_begin + 1, table_entry(tile_begin + 1), kw[1], vw[1], vsc[1], live[1]);
+    raw_ahead = table_entry(tile_begin + 2);
     if (live[0]) convert(0, kw[0], vw[0], vsc[0]);
     __syncthreads();                                              // Q' and the first tile are in place
     for (int tile = tile_begin; tile < tile_end; tile += 2) {
@@ -702,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
                     dst[8 * j + t + 4] = __float2half_rn(o[j][2 * hfr + 1] * inv);
                 }
             } else {
-                float* dst = part + (int64_t(split) * rows_valid + row) * (D + 2);
+                float* dst = part + (int64_t(split) * rows_valid + row) * part_row(D);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     __stcg(dst + 8 * j + t, o[j][2 * hfr]);
@@ -721,28 +772,12 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     __syncthreads();
     if (s_ticket != splits - 1) return;
     __threadfence();
-    for (int e = tid; e < rows_valid * (D / 2); e += kThreads) {
-        const int row = e / (D / 2), d = (e % (D / 2)) * 2;           // rows of D + 2 floats are 8-byte aligned
-        float mx = -INFINITY;
-        for (int sp = 0; sp < splits; ++sp)
-            mx = fmaxf(mx, __ldcg(part + (int64_t(sp) * rows_valid + row) * (D + 2) + D));
-        const float safe = mx == -INFINITY ? 0.f : mx;
-        float acc0 = 0.f, acc1 = 0.f, den = 0.f;
-        for (int sp = 0; sp < splits; ++sp) {
-            const float* src = part + (int64_t(sp) * rows_valid + row) * (D + 2);
-            const float m_sp = __ldcg(src + D);
-            if (m_sp == -INFINITY) continue;                          // an idle split wrote no sums
-            const float f = ex2(m_sp - safe);
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(src + d));
-            acc0 += v.x * f;
-            acc1 += v.y * f;
-            den += __ldcg(src + D + 1) * f;
-        }
-        const int mrow = row / rep, head = kvh * rep + row % rep;
-        const float inv = 1.f / fmaxf(den, 1e-20f);
-        *reinterpret_cast<__half2*>(p.out + (int64_t(seq * p.m + mrow) * p.hq + head) * D + d) =
-            __floats2half2_rn(acc0 * inv, acc1 * inv);
-    }
+    // the tile buffers are idle now: 64 rows x 64 splits pairs fit in them
+    merge_splits<D, kThreads>(
+        1, rows_valid, splits, reinterpret_cast<float2*>(sm_k), [&](int) { return part; },
+        [&](int, int row, int d, const float4& acc, float inv) {
+            store_h4(p.out + (int64_t(seq * p.m + row / rep) * p.hq + kvh * rep + row % rep) * D + d, acc, inv);
+        });
     if (tid == 0) *counter = 0;
 }
 
@@ -1210,7 +1245,7 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
             *reinterpret_cast<uint2*>(p.out + (int64_t(seq * p.m + mrow) * p.hq + qh) * D + d) =
                 make_uint2(h2_as_u32(h01), h2_as_u32(h23));
         } else {
-            float* dst = p.partial + ((int64_t(seq * p.hkv + head) * splits + split) * rows_valid + row) * (D + 2);
+            float* dst = p.partial + ((int64_t(seq * p.hkv + head) * splits + split) * rows_valid + row) * part_row(D);
 #pragma unroll
             for (int i = 0; i < 4; ++i) __stcg(dst + d + i, acc[i]);
             if (d == 0) { __stcg(dst + D, mx); __stcg(dst + D + 1, den); }
@@ -1225,29 +1260,14 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
     __syncthreads();
     if (s_ticket != splits - 1) return;
     __threadfence();
-    for (int e = tid; e < hpc * rows_valid * D4; e += kFastThreads) {
-        const int d = (e % D4) * 4, hr = e / D4;
-        const int hl = hr / rows_valid, row = hr - hl * rows_valid;
-        const int head = blockIdx.y * hpc + hl;
-        const float* part = p.partial + (int64_t(seq * p.hkv + head) * splits) * rows_valid * (D + 2);
-        float mx = -INFINITY;
-        for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, __ldcg(part + (int64_t(sp) * rows_valid + row) * (D + 2) + D));
-        const float safe = mx == -INFINITY ? 0.f : mx;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        float den = 0.f;
-        for (int sp = 0; sp < splits; ++sp) {
-            const float* src = part + (int64_t(sp) * rows_valid + row) * (D + 2);
-            const float f = ex2(__ldcg(src + D) - safe);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] += __ldcg(src + d + i) * f;
-            den += __ldcg(src + D + 1) * f;
-        }
-        const int mrow = row / rep, qh = head * rep + row % rep;
-        const float inv = 1.f / fmaxf(den, 1e-20f);
-        __half2 h01 = __floats2half2_rn(acc[0] * inv, acc[1] * inv), h23 = __floats2half2_rn(acc[2] * inv, acc[3] * inv);
-        *reinterpret_cast<uint2*>(p.out + (int64_t(seq * p.m + mrow) * p.hq + qh) * D + d) =
-            make_uint2(h2_as_u32(h01), h2_as_u32(h23));
-    }
+    __syncthreads();                                   // the per-warp results in shared memory are consumed
+    merge_splits<D, kFastThreads>(
+        hpc, rows_valid, splits, reinterpret_cast<float2*>(fsm),
+        [&](int hl) { return p.partial + (int64_t(seq * p.hkv + blockIdx.y * hpc + hl) * splits) * rows_valid * part_row(D); },
+        [&](int hl, int row, int d, const float4& acc, float inv) {
+            const int head = blockIdx.y * hpc + hl;
+            store_h4(p.out + (int64_t(seq * p.m + row / rep) * p.hq + head * rep + row % rep) * D + d, acc, inv);
+        });
     if (tid == 0) *counter = 0;
 }
 
@@ -1293,12 +1313,14 @@ int kv4_attention_splits(int batch, int m, int hq, int hkv, int d, int page, int
     const int base = batch * (hkv / hpc);
     int64_t splits = (fast ? 2 : 4) * kNumSMs / base;    // floor: the grid stays within one resident wave
     int64_t by_len = cdiv64(capacity, int64_t(1024) * wt);
-    // The verify kernel (one CTA walks its tokens alone, three CTAs per SM) is compute-bound and its grid
-    // usually exceeds one wave: short CTAs (256 tokens) let the block scheduler level the SMs, so the last
-    // wave costs 8 tiles instead of a whole split.
+    // The verify kernel (one CTA walks its tokens alone, three CTAs per SM) is compute-bound.  Measured at
+    // Qwen3-8B geometry with 2.2 k and 4.5 k tokens and batch 16 / 32 / 64, the time is flat within 5 % over
+    // grids of two to three resident waves and rises outside: about 1024 CTAs, none shorter than 512 tokens.
     if (!fast && d == 128 && row_tiles(m, hq, hkv) >= 2 && page % kVTile == 0) {
-        splits = cdiv64(3 * kNumSMs, base);
-        by_len = cdiv64(capacity, 256);
+        splits = cdiv64(1024, base);
+        by_len = 1;
+        const int64_t longest = capacity / 512 > 0 ? capacity / 512 : 1;
+        if (splits > longest) splits = longest;
     }
     if (by_len > splits) splits = by_len;
     const int64_t most = capacity / 256 > 0 ? capacity / 256 : 1;
@@ -1311,7 +1333,7 @@ int kv4_attention_splits(int batch, int m, int hq, int hkv, int d, int page, int
 size_t kv4_attention_workspace_bytes(int batch, int m, int hq, int hkv, int d, int page, int max_blocks) {
     const int splits = kv4_attention_splits(batch, m, hq, hkv, d, page, max_blocks);
     size_t bytes = size_t(kMaxCounters) * sizeof(int);
-    if (splits > 1) bytes += size_t(batch) * hq * m * splits * (d + 2) * sizeof(float);
+    if (splits > 1) bytes += size_t(batch) * hq * m * splits * part_row(d) * sizeof(float);
     return bytes;
 }
 

@@ -183,6 +183,7 @@ def ours_generate(quantized, kscale, kw, prompt, new_tokens, max_len):
     shape = (kw["num_hidden_layers"], kw["num_key_value_heads"], kw["head_dim"])
     runner = ModelRunner(model, rc, smooth_kv={"lambda": torch.ones(shape), "kscale": torch.full(shape, kscale)},
                          device="cuda:0")
+    runner.keep_logits = True
     seq = Sequence(list(prompt), 256)
     BlockPool(blocks).ensure(seq, len(prompt) + new_tokens + 8)
     first = runner.run([seq], True)

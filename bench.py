@@ -340,8 +340,9 @@ def self_check(tp, device):
     out = [[t] for t in first]
     for s, t in zip(seqs, first):
         s.append(t)
-    for _ in range(new_tokens - 1):
-        step = runner.run(seqs, False)
+    for i in range(new_tokens - 1):
+        runner.keep_logits = i == new_tokens - 2          # the tokens come from the pair exchange; the last
+        step = runner.run(seqs, False)                    # step also gathers the logits for the comparison
         for s, o, t in zip(seqs, out, step):
             s.append(t)
             o.append(t)

@@ -190,6 +190,48 @@ int lq2_kv4_attention(const void* q, int64_t q_row_stride, const uint32_t* kq, c
                       void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Attention of blocks of new rows over the pool-resident prefix only: every row of block b attends to
+ * positions [0, prefix_lens[b]) of the block table row b, with no causal step between the rows, and the
+ * natural-log sum of exp(scaled scores) of each row is returned beside the normalised output so that the
+ * caller can merge it with the attention over the rows' own (fp16) keys.  This is the pool half of the
+ * chunked-prefill attention that the reference builds from materialize_kv + torch.cat + flash-attn
+ * (qslab/runtime/model/attention.py:38-56,119-131): the prefix is read as int4 and never written back
+ * as fp16.
+ *
+ *   q             [blocks*rows, HQ, D] fp16, row stride q_row_stride elements
+ *   block_tables  [blocks, max_blocks] int32 (the sequence's row, repeated for each of its blocks)
+ *   prefix_lens   [blocks] int32
+ *   out           [blocks*rows, HQ, D] fp16;  lse [blocks*rows, HQ] fp32 (-inf for a row without keys)
+ * rows*HQ/HKV must be in 9..64; workspace as for lq2_kv4_attention with (blocks, rows) in place of
+ * (batch, verify_m).
+ */
+int lq2_kv4_attention_prefix(const void* q, int64_t q_row_stride, const uint32_t* kq, const void* ks,
+                             const uint32_t* vq, const void* vs, const int32_t* block_tables,
+                             const int32_t* prefix_lens, void* out, float* lse, int blocks, int rows,
+                             int hq, int hkv, int d, int page, int max_blocks, int v_group,
+                             int64_t num_slots, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Causal attention of a prefill step's new rows over the fp16 K/V of the same step, merged with the
+ * prefix part that lq2_kv4_attention_prefix returned; with it, the step's attention no longer needs the
+ * restored fp16 prefix nor the flash-attn call of qslab/runtime/model/attention.py:119-131.
+ *
+ *   q [rows, HQ, D], k, v [rows, HKV, D] fp16, row strides in elements (views into a fused projection
+ *       output are fine: k rows 16-byte aligned, v rows 8-byte aligned)
+ *   first_row   [rows] int32: first row of the step that belongs to the same sequence; row i attends to
+ *               rows first_row[i] .. i
+ *   prefix_row  [rows] int32: row of (pre, pre_lse) that holds this row's prefix part, -1 when its sequence
+ *               has no prefix, -2 to leave the row of `out` untouched
+ *   pre [*, HQ, D] fp16, pre_lse [*, HQ] fp32 (natural log); may be NULL when no row refers to them
+ *   out [rows, HQ, D] fp16 contiguous
+ * D is 64 or 128, HQ / HKV at most 8.
+ */
+int lq2_chunk_attention(const void* q, int64_t q_row_stride, const void* k, int64_t k_row_stride, const void* v,
+                        int64_t v_row_stride, const int32_t* first_row, const int32_t* prefix_row,
+                        const void* pre, const float* pre_lse, void* out, int rows, int hq, int hkv, int d,
+                        void* stream);
+
+/*
  * lq2_kv4_attention for callers that cannot allocate device memory.  It has no
  * counterpart in the reference.
  *

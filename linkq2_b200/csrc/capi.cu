@@ -18,8 +18,10 @@ int kv4_materialize_launch(const uint32_t*, const __half*, const uint32_t*, cons
 int kv4_attention_splits(int, int, int, int, int, int, int);
 size_t kv4_attention_workspace_bytes(int, int, int, int, int, int, int);
 int kv4_attention_launch(const __half*, int64_t, const uint32_t*, const __half*, const uint32_t*,
-                         const __half*, const int32_t*, const int32_t*, __half*, int, int, int, int, int,
+                         const __half*, const int32_t*, const int32_t*, __half*, float*, int, int, int, int, int, int,
                          int, int, int, int64_t, void*, size_t, cudaStream_t);
+int chunk_attention_launch(const __half*, int64_t, const __half*, int64_t, const __half*, int64_t, const int32_t*,
+                           const int32_t*, const __half*, const float*, __half*, int, int, int, int, cudaStream_t);
 size_t kv4_attention_builtin_scratch_bytes();
 int kv4_attention_builtin_scratch(void**);
 size_t kv4_attention_counter_bytes(int, int);
@@ -194,9 +196,44 @@ int lq2_kv4_attention(const void* q, int64_t q_row_stride, const uint32_t* kq, c
     if (!aligned(kq, 16) || !aligned(vq, 16) || !aligned(q, 2) || !aligned(workspace, 16)) return LQ2_ERR_ALIGN;
     return kv4_attention_launch(static_cast<const __half*>(q), q_row_stride, kq,
                                 static_cast<const __half*>(ks), vq, static_cast<const __half*>(vs),
-                                block_tables, context_lens, static_cast<__half*>(out), batch, verify_m, hq,
+                                block_tables, context_lens, static_cast<__half*>(out), nullptr, 1, batch, verify_m, hq,
                                 hkv, d, page, max_blocks, v_group, num_slots, workspace, workspace_bytes,
                                 static_cast<cudaStream_t>(stream));
+}
+
+int lq2_kv4_attention_prefix(const void* q, int64_t q_row_stride, const uint32_t* kq, const void* ks,
+                             const uint32_t* vq, const void* vs, const int32_t* block_tables,
+                             const int32_t* prefix_lens, void* out, float* lse, int blocks, int rows, int hq,
+                             int hkv, int d, int page, int max_blocks, int v_group, int64_t num_slots,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+    if (blocks == 0) return LQ2_OK;
+    if (!q || !kq || !ks || !vq || !vs || !block_tables || !prefix_lens || !out || !lse || num_slots <= 0)
+        return LQ2_ERR_ARG;
+    if (!attn_shape_ok(blocks, rows, hq, hkv, d, page, max_blocks)) return LQ2_ERR_SHAPE;
+    if (rows * (hq / hkv) <= 8) return LQ2_ERR_SHAPE;          // blocks of at least 9 query rows per KV head
+    if (v_group < d / 8 || !pow2(v_group) || d % v_group || num_slots < page) return LQ2_ERR_SHAPE;
+    if (!aligned(kq, 16) || !aligned(vq, 16) || !aligned(q, 2) || !aligned(workspace, 16) || !aligned(lse, 4))
+        return LQ2_ERR_ALIGN;
+    return kv4_attention_launch(static_cast<const __half*>(q), q_row_stride, kq,
+                                static_cast<const __half*>(ks), vq, static_cast<const __half*>(vs),
+                                block_tables, prefix_lens, static_cast<__half*>(out), lse, 0, blocks, rows, hq,
+                                hkv, d, page, max_blocks, v_group, num_slots, workspace, workspace_bytes,
+                                static_cast<cudaStream_t>(stream));
+}
+
+int lq2_chunk_attention(const void* q, int64_t q_row_stride, const void* k, int64_t k_row_stride, const void* v,
+                        int64_t v_row_stride, const int32_t* first_row, const int32_t* prefix_row, const void* pre,
+                        const float* pre_lse, void* out, int rows, int hq, int hkv, int d, void* stream) {
+    if (rows == 0) return LQ2_OK;
+    if (!q || !k || !v || !first_row || !prefix_row || !out || rows < 0) return LQ2_ERR_ARG;
+    if ((d != 64 && d != 128) || hkv <= 0 || hq <= 0 || hq % hkv || hq / hkv > 8) return LQ2_ERR_SHAPE;
+    if (k_row_stride % 8 || v_row_stride % 4 || !aligned(k, 16) || !aligned(v, 8) || !aligned(q, 2) ||
+        !aligned(out, 4) || !aligned(pre, 4) || !aligned(pre_lse, 4))
+        return LQ2_ERR_ALIGN;
+    return chunk_attention_launch(static_cast<const __half*>(q), q_row_stride, static_cast<const __half*>(k),
+                                  k_row_stride, static_cast<const __half*>(v), v_row_stride, first_row, prefix_row,
+                                  static_cast<const __half*>(pre), pre_lse, static_cast<__half*>(out), rows, hq, hkv,
+                                  d, static_cast<cudaStream_t>(stream));
 }
 
 size_t lq2_kv4_attention_static_max_bytes(void) { return kv4_attention_builtin_scratch_bytes(); }

@@ -62,7 +62,15 @@ struct AttnParams {
     float sl2;  // D^-0.5 * log2(e)
     float* partial;
     int* counters;
+    // Row m of a sequence reads positions [0, len + m * pos_step): 1 for decode / verify (causal over the
+    // drafts), 0 when all rows of a block attend to the same cached prefix (chunked prefill).
+    int pos_step;
+    float* lse;        // optional [batch * m, hq]: natural-log sum of exp(scores) per row, -inf without keys
 };
+
+__device__ __forceinline__ float lse_of(float max2, float den) {     // from the base-2 running maximum
+    return den > 0.f ? (max2 + log2f(den)) * 0.6931471805599453f : -INFINITY;
+}
 
 template <int D>
 struct KWords;
@@ -141,7 +149,7 @@ __device__ __forceinline__ void merge_splits(int units, int rows, int splits, fl
             for (int k = 0; k < 4; ++k) add(v[k], st[(sp + k) * rows]);
         }
         for (; sp < splits; ++sp) add(__ldcg(reinterpret_cast<const float4*>(src + sp * step)), st[sp * rows]);
-        store(u, row, d, acc, 1.f / fmaxf(den, 1e-20f));
+        store(u, row, d, acc, 1.f / fmaxf(den, 1e-20f), lse_of(safe, den));
     }
 }
 
@@ -179,7 +187,7 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
 
     const int capacity = p.max_blocks * p.page;
     const int len = p.lens[seq];
-    const int reach = min(len + p.m - 1, capacity);          // keys any row of this sequence reads
+    const int reach = min(len + (p.m - 1) * p.pos_step, capacity);   // keys any row of this sequence reads
     const int tiles = reach > 0 ? (reach + kTile - 1) / kTile : 0;
     const int per_split = (tiles + p.splits - 1) / p.splits;
     const int tile_begin = split * per_split;
@@ -189,8 +197,8 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
     const int r_lo = 16 * rt + g, r_hi = r_lo + 8;
     const bool v_lo = r_lo < rows_valid, v_hi = r_hi < rows_valid;
     const int m_lo = v_lo ? r_lo / rep : 0, m_hi = v_hi ? r_hi / rep : 0;
-    const int lim_lo = v_lo ? min(len + m_lo, capacity) : 0;
-    const int lim_hi = v_hi ? min(len + m_hi, capacity) : 0;
+    const int lim_lo = v_lo ? min(len + m_lo * p.pos_step, capacity) : 0;
+    const int lim_hi = v_hi ? min(len + m_hi * p.pos_step, capacity) : 0;
     // Q' = q * ks is exact in fp32 and is carried as a high and a low fp16 part (two MMAs per operand):
     // rounded to one fp16 it would shift every score of a row by the same channel-wise error, which
     // does not average out over the tokens.
@@ -402,6 +410,7 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
         if (splits == 1) {
             const int mrow = row / rep, head = kvh * rep + row % rep;
             p.out[(int64_t(seq * p.m + mrow) * p.hq + head) * D + d] = __float2half_rn(acc / fmaxf(den, 1e-20f));
+            if (d == 0 && p.lse) p.lse[int64_t(seq * p.m + mrow) * p.hq + head] = lse_of(safe, den);
         } else {
             float* dst = part + (int64_t(split) * rows_valid + row) * part_row(D);
             __stcg(dst + d, acc);
@@ -419,8 +428,9 @@ __global__ void __launch_bounds__(kThreads) kv4_attention_kernel(const AttnParam
     __threadfence();
     merge_splits<D, kThreads>(
         1, rows_valid, splits, reinterpret_cast<float2*>(sm_raw), [&](int) { return part; },
-        [&](int, int row, int d, const float4& acc, float inv) {
+        [&](int, int row, int d, const float4& acc, float inv, float lse) {
             store_h4(p.out + (int64_t(seq * p.m + row / rep) * p.hq + kvh * rep + row % rep) * D + d, acc, inv);
+            if (d == 0 && p.lse) p.lse[int64_t(seq * p.m + row / rep) * p.hq + kvh * rep + row % rep] = lse;
         });
     if (tid == 0) *counter = 0;
 }
@@ -485,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
 
     const int capacity = p.max_blocks * p.page;
     const int len = p.lens[seq];
-    const int reach = min(len + p.m - 1, capacity);
+    const int reach = min(len + (p.m - 1) * p.pos_step, capacity);
     const int tiles = reach > 0 ? (reach + kVTile - 1) / kVTile : 0;
     const int per_split = (tiles + p.splits - 1) / p.splits;
     const int tile_begin = split * per_split;
@@ -537,8 +547,8 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     const bool mma_warp = warp < RT;
     const int r_lo = 16 * warp + g, r_hi = r_lo + 8;
     const bool v_lo = mma_warp && r_lo < rows_valid, v_hi = mma_warp && r_hi < rows_valid;
-    const int lim_lo = v_lo ? min(len + r_lo / rep, capacity) : 0;
-    const int lim_hi = v_hi ? min(len + r_hi / rep, capacity) : 0;
+    const int lim_lo = v_lo ? min(len + r_lo / rep * p.pos_step, capacity) : 0;
+    const int lim_hi = v_hi ? min(len + r_hi / rep * p.pos_step, capacity) : 0;
     int lim_min = min(lim_lo, lim_hi);                        // tiles wholly below it need no mask
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) lim_min = min(lim_min, __shfl_xor_sync(0xffffffffu, lim_min, off));
@@ -752,6 +762,8 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
                     dst[8 * j + t] = __float2half_rn(o[j][2 * hfr] * inv);
                     dst[8 * j + t + 4] = __float2half_rn(o[j][2 * hfr + 1] * inv);
                 }
+                if (t == 0 && p.lse)
+                    p.lse[int64_t(seq * p.m + row / rep) * p.hq + kvh * rep + row % rep] = lse_of(mx, den);
             } else {
                 float* dst = part + (int64_t(split) * rows_valid + row) * part_row(D);
 #pragma unroll
@@ -775,8 +787,9 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     // the tile buffers are idle now: 64 rows x 64 splits pairs fit in them
     merge_splits<D, kThreads>(
         1, rows_valid, splits, reinterpret_cast<float2*>(sm_k), [&](int) { return part; },
-        [&](int, int row, int d, const float4& acc, float inv) {
+        [&](int, int row, int d, const float4& acc, float inv, float lse) {
             store_h4(p.out + (int64_t(seq * p.m + row / rep) * p.hq + kvh * rep + row % rep) * D + d, acc, inv);
+            if (d == 0 && p.lse) p.lse[int64_t(seq * p.m + row / rep) * p.hq + kvh * rep + row % rep] = lse;
         });
     if (tid == 0) *counter = 0;
 }
@@ -1264,7 +1277,7 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
     merge_splits<D, kFastThreads>(
         hpc, rows_valid, splits, reinterpret_cast<float2*>(fsm),
         [&](int hl) { return p.partial + (int64_t(seq * p.hkv + blockIdx.y * hpc + hl) * splits) * rows_valid * part_row(D); },
-        [&](int hl, int row, int d, const float4& acc, float inv) {
+        [&](int hl, int row, int d, const float4& acc, float inv, float) {
             const int head = blockIdx.y * hpc + hl;
             store_h4(p.out + (int64_t(seq * p.m + row / rep) * p.hq + head * rep + row % rep) * D + d, acc, inv);
         });
@@ -1362,7 +1375,7 @@ size_t kv4_attention_counter_bytes(int batch, int hkv) { return size_t(batch) * 
 
 int kv4_attention_launch(const __half* q, int64_t q_stride, const uint32_t* kq, const __half* ks,
                          const uint32_t* vq, const __half* vs, const int32_t* bt, const int32_t* lens,
-                         __half* out, int batch, int m, int hq, int hkv, int d, int page, int max_blocks,
+                         __half* out, float* lse, int pos_step, int batch, int m, int hq, int hkv, int d, int page, int max_blocks,
                          int v_group, int64_t num_slots, void* workspace, size_t workspace_bytes,
                          cudaStream_t st) {
     if (batch * hkv > kMaxCounters) return LQ2_ERR_SHAPE;
@@ -1370,6 +1383,7 @@ int kv4_attention_launch(const __half* q, int64_t q_stride, const uint32_t* kq, 
         return LQ2_ERR_WORKSPACE;
     AttnParams p;
     p.q = q; p.q_stride = q_stride; p.kq = kq; p.ks = ks; p.vq = vq; p.vs = vs; p.bt = bt; p.lens = lens;
+    p.lse = lse; p.pos_step = pos_step;
     p.out = out; p.batch = batch; p.m = m; p.hq = hq; p.hkv = hkv; p.page = page; p.max_blocks = max_blocks;
     p.ng = d / v_group;
     int shift = 0;
@@ -1383,7 +1397,7 @@ int kv4_attention_launch(const __half* q, int64_t q_stride, const uint32_t* kq, 
     p.sl2 = float(1.4426950408889634 / sqrt(double(d)));
     p.counters = reinterpret_cast<int*>(workspace);
     p.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + size_t(kMaxCounters) * sizeof(int));
-    if (fast_path_ok(m, hq, hkv, d, page, p.ng)) {
+    if (fast_path_ok(m, hq, hkv, d, page, p.ng) && pos_step == 1 && !lse) {
         const int hpc = fast_heads_per_cta(batch, hkv, int64_t(max_blocks) * page);
         dim3 fgrid(p.splits, hkv / hpc, batch);
         static bool configured[64] = {};

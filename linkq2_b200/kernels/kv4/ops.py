@@ -99,6 +99,83 @@ def paged_attention_decode(q: torch.Tensor, k_cache, v_cache, block_tables: torc
     return out
 
 
+def paged_attention_prefix(q: torch.Tensor, k_cache, v_cache, block_tables: torch.Tensor,
+                           prefix_lens: torch.Tensor, block_n: int = 128, num_kv_heads: int | None = None,
+                           v_group: int = 64, rows: int = 16):
+    """Attention of blocks of ``rows`` new query rows over the pool-resident prefix only:
+    ``q [blocks*rows, HQ, D] fp16 -> (out [blocks*rows, HQ, D] fp16, lse [blocks*rows, HQ] fp32)``.
+    Every row of block ``b`` attends to positions ``[0, prefix_lens[b])`` of ``block_tables[b]``;
+    ``lse`` is the natural-log sum of exp(scaled scores), ``-inf`` for an empty prefix.  The int4
+    half of chunked prefill, for which the reference restores the prefix to fp16 first
+    (``qslab/runtime/model/attention.py:38-56,119-131``)."""
+    total, hq, d = q.shape
+    hkv = num_kv_heads if num_kv_heads is not None else hq
+    kq, ks = k_cache
+    vq, vs = v_cache
+    if q.dtype != torch.float16:
+        raise TypeError("KV4 attention takes fp16 queries")
+    _static_scale(ks, hkv, d)
+    if total % rows:
+        raise ValueError("the query rows must come in whole blocks")
+    out = torch.empty((total, hq, d), dtype=torch.float16, device=q.device)
+    lse = torch.empty((total, hq), dtype=torch.float32, device=q.device)
+    if total == 0:
+        return out, lse
+    blocks = total // rows
+    if q.stride(2) != 1 or q.stride(1) != d:
+        q = q.contiguous()
+    bt = block_tables if block_tables.dtype == torch.int32 else block_tables.to(torch.int32)
+    bt = bt if bt.is_contiguous() else bt.contiguous()
+    lens = prefix_lens if prefix_lens.dtype == torch.int32 else prefix_lens.to(torch.int32)
+    max_blocks = bt.shape[1]
+    args = (blocks, rows, hq, hkv, d, block_n, max_blocks)
+    with torch.cuda.device(q.device):
+        need = _lib.lib.lq2_kv4_attention_workspace_bytes(*args)
+        if need == 0:
+            raise ValueError(f"unsupported KV4 prefix attention shape: blocks={blocks} rows={rows} HQ={hq} "
+                             f"HKV={hkv} D={d} page={block_n} table={max_blocks}")
+        ws = _workspace.get("kv4", need, q.device)
+        stream = torch.cuda.current_stream().cuda_stream
+        status = _lib.lib.lq2_kv4_attention_prefix(
+            q.data_ptr(), q.stride(0), kq.data_ptr(), ks.data_ptr(), vq.data_ptr(), vs.data_ptr(),
+            bt.data_ptr(), lens.data_ptr(), out.data_ptr(), lse.data_ptr(), blocks, rows, hq, hkv, d, block_n,
+            max_blocks, v_group, kq.shape[0], ws.data_ptr(), ws.numel(), stream)
+    _lib.check(status, "lq2_kv4_attention_prefix")
+    _lib.count()
+    return out, lse
+
+
+def chunk_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, first_row: torch.Tensor,
+                    prefix_row: torch.Tensor, pre: torch.Tensor | None = None,
+                    pre_lse: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of a prefill step's new rows ``q [T, HQ, D]`` over the step's own fp16
+    ``k, v [T, HKV, D]`` (row ``i`` sees rows ``first_row[i] .. i``), merged with the prefix part
+    ``(pre, pre_lse)`` of ``paged_attention_prefix`` at row ``prefix_row[i]`` (``-1``: no prefix,
+    ``-2``: leave ``out[i]`` alone).  Stands in for the flash-attn call of
+    ``qslab/runtime/model/attention.py:119-131``."""
+    t, hq, d = q.shape
+    hkv = k.shape[1]
+    if q.dtype != torch.float16 or k.dtype != torch.float16 or v.dtype != torch.float16:
+        raise TypeError("chunk attention takes fp16 q, k, v")
+    out = torch.empty((t, hq, d), dtype=torch.float16, device=q.device) if out is None else out
+    if t == 0:
+        return out
+    def rows_of(x, heads):
+        return x if x.stride(2) == 1 and x.stride(1) == d else x.contiguous()
+    q, k, v = rows_of(q, hq), rows_of(k, hkv), rows_of(v, hkv)
+    first_row = first_row.to(torch.int32)
+    prefix_row = prefix_row.to(torch.int32)
+    with torch.cuda.device(q.device):
+        status = _lib.lib.lq2_chunk_attention(
+            q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), first_row.data_ptr(),
+            prefix_row.data_ptr(), pre.data_ptr() if pre is not None else None,
+            pre_lse.data_ptr() if pre_lse is not None else None, out.data_ptr(), t, hq, hkv, d,
+            torch.cuda.current_stream().cuda_stream)
+    _lib.check(status, "lq2_chunk_attention")
+    _lib.count()
+    return out
+
+
 def materialize_kv(k_cache, v_cache, slots: torch.Tensor, v_group: int = 64):
     """Dequantise the selected slots to fp16 ``[T, HKV, D]`` (prefix restore,
     ``qslab/kernels/kv4/layout.py:33-47``)."""

@@ -16,6 +16,7 @@ import torch
 
 from linkq2_b200.kernels.gemlite.ops import set_constant_weights
 from linkq2_b200.runtime.execute.cuda_graph import CUDAGraphs
+from linkq2_b200.runtime.model.attention import LONG_PROMPT
 from linkq2_b200.runtime.model.context import get_context, reset_context, set_context
 from linkq2_b200.runtime.parallel import get_tp
 from linkq2_b200.runtime.state import Sequence
@@ -43,6 +44,9 @@ class ModelRunner:
         self.tp = get_tp()
         self.graph_replays = 0
         self.last_logits = None
+        self.keep_logits = False          # True: every step also gathers the full logits into last_logits
+        self.temperature = 0.0            # 0: greedy; a float or one value per row
+        self.sample_generator = None      # torch.Generator on the device, for seeded sampling
         self._pinned = self._pinned_np = self._packed_dev = None
         self.allocate_kv_cache()
         self.load_smoothing(smooth_kv)
@@ -152,27 +156,51 @@ class ModelRunner:
                     block_tables=self.prepare_block_tables(seqs), verify_m=m_rows)
         return self._h2d(ids, torch.int64), self._h2d(pos, torch.int64)
 
+    def _prefix_rows(self) -> int:
+        """Query rows per block of the KV4 prefix kernel: 16, fewer when the GQA group is wider than
+        four heads (the kernel holds at most 64 rows per KV head)."""
+        cfg = self.model.config
+        return max(1, min(16, 64 // max(1, cfg.num_attention_heads // cfg.num_key_value_heads)))
+
     def prepare_prefill(self, seqs: list[Sequence], counts: list[int]):
-        """Schedule ``counts[i]`` prompt tokens of each sequence after its cached prefix."""
+        """Schedule ``counts[i]`` prompt tokens of each sequence after its cached prefix.  The
+        prefix stays in the int4 pool: the new rows are cut into blocks for the prefix kernel
+        (the reference restores the prefix to fp16 instead,
+        ``qslab/runtime/execute/model_runner.py:232-263``)."""
         ids, pos, slots, cu_q, cu_k = [], [], [], [0], [0]
-        prefix_slots, plan, q_off = [], [], 0
-        for seq, n in zip(seqs, counts):
+        plan, q_off = [], 0
+        rows, block_seq, lens, first, where = [], [], [], [], []
+        r = self._prefix_rows()
+        for i, (seq, n) in enumerate(zip(seqs, counts)):
             start, end = seq.num_cached_tokens, seq.num_cached_tokens + n
             ids.extend(seq.token_ids[start:end])
             pos.extend(range(start, end))
             slots.extend(seq.slot(p) for p in range(start, end))
             cu_q.append(cu_q[-1] + n)
             cu_k.append(cu_k[-1] + end)
-            plan.append((len(prefix_slots), start, q_off, q_off + n, True))
-            prefix_slots.extend(seq.slot(p) for p in range(start))
+            plan.append((start, q_off, q_off + n))
+            first.extend([q_off] * n)
+            if start > 0:
+                for b0 in range(q_off, q_off + n, r):
+                    real = list(range(b0, min(b0 + r, q_off + n)))
+                    where.extend(range(len(rows), len(rows) + len(real)))
+                    rows.extend(real + [q_off] * (r - len(real)))
+                    block_seq.append(i)
+                    lens.append(start)
+            else:
+                where.extend([-1 if n <= LONG_PROMPT else -2] * n)
             q_off += n
-        has_prefix = cu_k[-1] > cu_q[-1]
+        extra = dict(prefix_plan=plan, chunk_first=self._h2d(first, torch.int32),
+                     chunk_prefix=self._h2d(where, torch.int32))
+        tables = None
+        if rows:
+            tables = self.prepare_block_tables(seqs)
+            extra.update(prefix_rows=self._h2d(rows, torch.int64),
+                         prefix_tables=tables[self._h2d(block_seq, torch.int64)].contiguous(),
+                         prefix_lens=self._h2d(lens, torch.int32))
         set_context(True, self._h2d(cu_q, torch.int32), self._h2d(cu_k, torch.int32),
-                    max(counts), max(c[1] + (c[3] - c[2]) for c in plan),
-                    self._h2d(slots, torch.int32), None,
-                    self.prepare_block_tables(seqs) if has_prefix else None,
-                    prefix_slots=self._h2d(prefix_slots, torch.int64) if has_prefix else None,
-                    prefix_plan=plan if has_prefix else None)
+                    max(counts), max(c[0] + (c[2] - c[1]) for c in plan),
+                    self._h2d(slots, torch.int32), None, tables, **extra)
         return self._h2d(ids, torch.int64), self._h2d(pos, torch.int64)
 
     # ---- execution ------------------------------------------------------------
@@ -294,8 +322,7 @@ class ModelRunner:
             bucket = graphs.stage_packed(staged[i], b, width)
             graphs.run_graph(1, bucket)
             self.graph_replays += 1
-            self.last_logits = self.model.compute_logits(graphs.families[1].buffers['outputs'][:b])
-            ids = self.last_logits.argmax(dim=-1)
+            ids = self._sample(graphs.families[1].buffers['outputs'][:b])
             tokens_host[i].copy_(ids, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         out = tokens_host.tolist()
@@ -309,10 +336,29 @@ class ModelRunner:
             hidden = hidden[(get_context().cu_seqlens_q[1:] - 1).long()]
             for seq, n in zip(seqs, counts):
                 seq.num_cached_tokens += n
-        self.last_logits = self.model.compute_logits(hidden)
-        tokens = self.last_logits.argmax(dim=-1).tolist()
+        tokens = self._sample(hidden).tolist()
         reset_context()
         return tokens
+
+    def _sample(self, hidden):
+        """Token ids for the rows of ``hidden``.  Greedy rows take the arg-max, which is found
+        without gathering the other tensor-parallel ranks' logits unless ``keep_logits`` asks
+        for them (``last_logits``).  Rows with a temperature above 1e-6 are drawn from
+        softmax(logits / temperature) by the exponential race of
+        ``qslab/runtime/execute/sampler.py:8-13``: arg-max of probs / Exp(1) noise."""
+        temps = torch.as_tensor(self.temperature, dtype=torch.float32, device=hidden.device)
+        if bool((temps > 1e-6).any()):
+            self.last_logits = self.model.compute_logits(hidden)
+            temps = temps.expand(hidden.shape[0]) if temps.dim() == 0 else temps
+            greedy = self.last_logits.argmax(dim=-1)
+            probs = torch.softmax(self.last_logits.float() / temps.clamp_min(1e-6).unsqueeze(1), dim=-1)
+            noise = torch.empty_like(probs).exponential_(1, generator=self.sample_generator).clamp_min_(1e-10)
+            return torch.where(temps <= 1e-6, greedy, (probs / noise).argmax(dim=-1))
+        if self.keep_logits:
+            self.last_logits = self.model.compute_logits(hidden)
+            return self.last_logits.argmax(dim=-1)
+        self.last_logits = None
+        return self.model.greedy_tokens(hidden)
 
     @torch.inference_mode()
     def verify(self, seqs: list[Sequence], drafts: list[list[int]]) -> list[list[int]]:
@@ -321,7 +367,7 @@ class ModelRunner:
         m_rows = self.config.spec_num_drafts + 1
         input_ids, positions = self.prepare_verify(seqs, drafts)
         hidden = self.run_model(input_ids, positions, False, rows=m_rows)
-        tokens = self.model.compute_logits(hidden).argmax(dim=-1).view(len(seqs), m_rows).tolist()
+        tokens = self.model.greedy_tokens(hidden).view(len(seqs), m_rows).tolist()
         reset_context()
         return tokens
 

@@ -2,11 +2,11 @@
 
 Mirror of ``PagedAttention`` (``qslab/runtime/model/attention.py:21-144``) for
 the KV4 cache: SmoothAttention scaling, store before attention, paged decode /
-verify through the KV4 kernels, and prefill over the fp16 rows of the step with
-the pool-resident prefix restored in front of them.  The reference runs prefill
-through the flash-attn wheel (``attention.py:121-131``); here it is torch's
-scaled_dot_product_attention per sequence — prefill attention is not part of
-the replaced path.  ``num_heads`` / ``num_kv_heads`` are this rank's shard.
+verify through the KV4 kernels, and prefill over the fp16 rows of the step plus
+the pool-resident prefix.  The reference restores the prefix to fp16 and runs
+both through the flash-attn wheel (``attention.py:38-56,121-131``); here the
+prefix is read as int4 by the KV4 prefix kernel and merged with the attention
+over the step's own rows.  ``num_heads`` / ``num_kv_heads`` are this rank's shard.
 """
 from __future__ import annotations
 
@@ -14,8 +14,11 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from linkq2_b200.kernels.kv4 import materialize_kv, paged_attention_decode, store_kv_quant
+from linkq2_b200.kernels.kv4 import paged_attention_decode, store_kv_quant
+from linkq2_b200.kernels.kv4.ops import chunk_attention, paged_attention_prefix
 from linkq2_b200.runtime.model.context import get_context
+
+LONG_PROMPT = 256     # rows of one sequence in one step beyond which torch's fused attention takes over
 
 
 class PagedAttention(nn.Module):
@@ -38,30 +41,26 @@ class PagedAttention(nn.Module):
         self.lam_q = self.lam.repeat_interleave(rep, dim=0).contiguous()
 
     def _prefill(self, ctx, q, k, v):
-        out = torch.empty_like(q)
-        if ctx.block_tables is not None and ctx.prefix_plan:
-            kp, vp = materialize_kv(self.k_cache, self.v_cache, ctx.prefix_slots, v_group=self.v_group)
-            plan = ctx.prefix_plan
-        else:
-            cu = ctx.cu_seqlens_q.tolist()
-            kp = vp = None
-            plan = [(0, 0, cu[i], cu[i + 1], True) for i in range(len(cu) - 1)]
-        for slot_off, cached, q0, q1, is_prefill in plan:
-            ks, vs = [], []
-            if cached > 0:
-                ks.append(kp[slot_off:slot_off + cached])
-                vs.append(vp[slot_off:slot_off + cached])
-            if is_prefill:
-                ks.append(k[q0:q1])
-                vs.append(v[q0:q1])
-            kk, vv = torch.cat(ks), torch.cat(vs)
-            tq, tk = q1 - q0, kk.shape[0]
-            # bottom-right aligned causal mask: query i sees keys [0, tk - tq + i]
-            mask = torch.ones(tq, tk, dtype=torch.bool, device=q.device).tril(diagonal=tk - tq)
-            o = F.scaled_dot_product_attention(
-                q[q0:q1].transpose(0, 1).unsqueeze(0), kk.transpose(0, 1).unsqueeze(0),
-                vv.transpose(0, 1).unsqueeze(0), attn_mask=mask, scale=self.scale, enable_gqa=True)
-            out[q0:q1] = o.squeeze(0).transpose(0, 1)
+        """Attention of the step's new rows: over themselves in fp16 (``chunk_attention``) and,
+        for sequences with rows already in the pool, over that prefix read as int4 by the KV4
+        prefix kernel; the first kernel merges the two parts by their softmax weights.  Replaces
+        materialize + cat + flash-attn (``qslab/runtime/model/attention.py:38-56,119-131``).
+        Only a prompt of more than 256 rows without prefix still goes through torch's fused
+        attention, which is what the reference uses there too."""
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        pre = pre_lse = None
+        if ctx.prefix_rows is not None:
+            pre, pre_lse = paged_attention_prefix(
+                q.index_select(0, ctx.prefix_rows), self.k_cache, self.v_cache, ctx.prefix_tables, ctx.prefix_lens,
+                block_n=self.block_n, num_kv_heads=self.num_kv_heads, v_group=self.v_group,
+                rows=ctx.prefix_rows.numel() // ctx.prefix_lens.numel())
+        chunk_attention(q, k, v, ctx.chunk_first, ctx.chunk_prefix, pre, pre_lse, out)
+        for cached, q0, q1 in ctx.prefix_plan:
+            if cached == 0 and q1 - q0 > LONG_PROMPT:
+                o = F.scaled_dot_product_attention(
+                    q[q0:q1].transpose(0, 1).unsqueeze(0), k[q0:q1].transpose(0, 1).unsqueeze(0),
+                    v[q0:q1].transpose(0, 1).unsqueeze(0), is_causal=True, scale=self.scale, enable_gqa=True)
+                out[q0:q1] = o.squeeze(0).transpose(0, 1)
         return out
 
     def attend(self, q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor):

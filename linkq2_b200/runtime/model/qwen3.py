@@ -202,6 +202,7 @@ class Qwen3ForCausalLM(nn.Module):
         self.lm_head = LMHead(config.vocab_size, config.hidden_size)
         if config.tie_word_embeddings:
             self.lm_head.weight = self.model.embed_tokens.weight
+        self.head_rows = None            # (first row, rows, vocabulary) once shard_head() has cut the head
 
     def fuse_projections(self):
         """Fuse q/k/v and gate/up of every layer into single W4 launches (a
@@ -215,17 +216,59 @@ class Qwen3ForCausalLM(nn.Module):
     def forward(self, input_ids, positions):
         return self.model(input_ids, positions)
 
-    def compute_logits(self, hidden_states):
-        """Logits over the whole vocabulary.  Under tensor parallelism each rank multiplies
-        by its slice of the (replicated) head only, a 1/t share of the 1.2 GB fp16 matrix
-        that is otherwise a quarter of a decode step's bytes, and the slices are gathered."""
+    def shard_head(self):
+        """Under tensor parallelism keep only this rank's slice of the vocabulary rows of an
+        untied LM head (1.2 GB of fp16 at Qwen3-8B size, replicated otherwise).  A head tied to
+        the embedding stays whole, because the embedding lookup needs every row, and is
+        sliced as a view at use.  Replaces the replicated head of
+        ``qslab/runtime/execute/model_runner.py:398``."""
+        tp = get_tp()
+        vocab = self.lm_head.weight.shape[0]
+        if tp.size == 1 or vocab % tp.size or self.config.tie_word_embeddings or self.head_rows is not None:
+            return self
+        share = vocab // tp.size
+        local = self.lm_head.weight.data[tp.rank * share:(tp.rank + 1) * share].clone()
+        self.lm_head.weight = nn.Parameter(local, requires_grad=False)
+        self.head_rows = (tp.rank * share, share, vocab)
+        return self
+
+    def _local_logits(self, hidden_states):
+        """``(logits of this rank's vocabulary slice, first row of the slice, vocabulary size)``;
+        the whole vocabulary when the head cannot be split evenly or there is one rank."""
         tp = get_tp()
         weight = self.lm_head.weight
+        if self.head_rows is not None:
+            first, _, vocab = self.head_rows
+            return F.linear(hidden_states, weight), first, vocab
         vocab = weight.shape[0]
         if tp.size == 1 or vocab % tp.size or not dist.is_initialized():
-            return self.lm_head(hidden_states)
+            return self.lm_head(hidden_states), 0, vocab
         share = vocab // tp.size
-        local = F.linear(hidden_states, weight[tp.rank * share:(tp.rank + 1) * share])
+        return F.linear(hidden_states, weight[tp.rank * share:(tp.rank + 1) * share]), tp.rank * share, vocab
+
+    def compute_logits(self, hidden_states):
+        """Logits over the whole vocabulary.  Under tensor parallelism each rank multiplies
+        by its slice of the head only and the slices are gathered (``greedy_tokens`` avoids the
+        gather when only the arg-max is wanted)."""
+        tp = get_tp()
+        local, _, vocab = self._local_logits(hidden_states)
+        if local.shape[-1] == vocab:
+            return local
         parts = torch.empty((tp.size,) + tuple(local.shape), dtype=local.dtype, device=local.device)
         dist.all_gather_into_tensor(parts, local.contiguous(), group=tp.group)
         return parts.movedim(0, -2).reshape(*local.shape[:-1], vocab)
+
+    def greedy_tokens(self, hidden_states):
+        """Arg-max token per row, equal to ``compute_logits(h).argmax(-1)`` (ties go to the lowest
+        index).  Under tensor parallelism the ranks exchange one (value, index) pair per row
+        instead of their logits: 8 bytes per row and rank against 2 * vocab / t."""
+        tp = get_tp()
+        local, first, vocab = self._local_logits(hidden_states)
+        if local.shape[-1] == vocab:
+            return local.argmax(dim=-1)
+        value, index = local.max(dim=-1)                      # index of the first maximum
+        pair = torch.stack([value.float(), (index + first).float()], dim=-1).contiguous()   # ids < 2**24: exact
+        pairs = torch.empty((tp.size,) + tuple(pair.shape), dtype=pair.dtype, device=pair.device)
+        dist.all_gather_into_tensor(pairs, pair, group=tp.group)
+        best = pairs[..., 0].argmax(dim=0, keepdim=True)      # first maximum: the lowest rank, so the lowest index
+        return pairs[..., 1].gather(0, best).squeeze(0).long()

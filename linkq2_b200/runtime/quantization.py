@@ -143,6 +143,7 @@ def build_from_checkpoint(path, *, device="cuda:0", max_position=None, fake=Fals
     load_checkpoint_weights(model, path, device=device, fake=fake)
     if not fake:
         model.fuse_projections()
+        model.shard_head()
     return model.eval()
 
 
@@ -207,6 +208,7 @@ def build_random(cfg: ModelConfig, *, seed=0, group_size=128, device="cuda:0", m
         if param.is_meta:                      # the RMSNorm weights
             _set_param(model, name, torch.ones(param.shape, dtype=torch.float16, device=dev))
     model.fuse_projections()
+    model.shard_head()
     return model.eval()
 
 

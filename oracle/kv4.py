@@ -6,7 +6,10 @@ Restates with torch CPU tensors:
 * ``paged_attention_decode`` for one query position and for the multi-position
   verify — ``qslab/kernels/kv4/paged_attention.py:11-150`` and
   ``qslab/kernels/kv4/grouped_attention.py:7-63``;
-* ``materialize_kv`` — ``qslab/kernels/kv4/layout.py:9-47``.
+* ``materialize_kv`` — ``qslab/kernels/kv4/layout.py:9-47``;
+* ``paged_attention_prefix`` — the pool half of chunked prefill, which the
+  reference composes from ``materialize_kv`` and flash-attn
+  (``qslab/runtime/model/attention.py:38-56,119-131``).
 
 Pool layout (``qslab/runtime/execute/model_runner.py:146-156``):
 ``kq, vq [S, HKV, D/8]`` 32-bit words, ``ks [HKV, D] fp16`` static per-channel
@@ -163,6 +166,65 @@ def paged_attention_decode(q, k_cache, v_cache, block_tables, context_lens,
             scores = scores.masked_fill(~valid.unsqueeze(0), float("-inf"))
             out[row] = torch.einsum("ht,htd->hd", torch.softmax(scores, -1), vh)
     return out.to(out_dtype)
+
+
+def paged_attention_prefix(q, k_cache, v_cache, block_tables, prefix_lens, block_n: int = 128,
+                           num_kv_heads: int | None = None, v_group: int = 64, rows: int = 16):
+    """The pool half of chunked-prefill attention: every row of block ``b`` (``rows`` rows of
+    ``q [blocks*rows, HQ, D]``) attends to the dequantised positions ``[0, prefix_lens[b])`` of
+    ``block_tables[b]``.  Returns fp32 ``(out, lse)``, ``lse`` the natural-log sum of
+    exp(scaled scores), ``-inf`` and zeros for an empty prefix.  The reference gets the same
+    numbers by restoring the prefix with ``materialize_kv`` and handing it to flash-attn in
+    front of the step's own rows (``qslab/runtime/model/attention.py:38-56,119-131``)."""
+    total, hq, d = q.shape
+    hkv = num_kv_heads if num_kv_heads is not None else hq
+    heads = torch.arange(hq) // (hq // hkv)
+    out = torch.zeros(total, hq, d, dtype=torch.float32)
+    lse = torch.full((total, hq), float("-inf"), dtype=torch.float32)
+    bt = block_tables.to(torch.int64)
+    for b in range(total // rows):
+        n = min(int(prefix_lens[b]), block_tables.shape[1] * block_n)
+        if n <= 0:
+            continue
+        pos = torch.arange(n)
+        raw = bt[b, pos // block_n]
+        keep = raw >= 0
+        if not bool(keep.any()):
+            continue
+        slots = (raw * block_n + pos % block_n)[keep]
+        k, v = dequantize_slots(k_cache, v_cache, slots, v_group)
+        qb = q[b * rows:(b + 1) * rows].float()
+        scores = torch.einsum("rhd,thd->rht", qb, k[:, heads]) * (d ** -0.5)
+        part = torch.logsumexp(scores, dim=-1)
+        lse[b * rows:(b + 1) * rows] = part
+        out[b * rows:(b + 1) * rows] = torch.einsum("rht,thd->rhd", torch.exp(scores - part.unsqueeze(-1)), v[:, heads])
+    return out, lse
+
+
+def chunk_attention(q, k, v, first_row, prefix_row, pre=None, pre_lse=None):
+    """Causal attention of a step's new rows over the step's own fp16 ``k, v`` (row ``i`` sees
+    rows ``first_row[i] .. i``), merged with the prefix part ``pre[prefix_row[i]]`` weighted by
+    ``exp(pre_lse)`` against the own part's sum of exponentials; fp32 ``[T, HQ, D]``, rows with
+    ``prefix_row == -2`` left at zero.  Together with ``paged_attention_prefix`` this is the
+    softmax over prefix + own keys that the reference computes in one flash-attn call
+    (``qslab/runtime/model/attention.py:119-131``)."""
+    t, hq, d = q.shape
+    heads = torch.arange(hq) // (hq // k.shape[1])
+    out = torch.zeros(t, hq, d, dtype=torch.float32)
+    for i in range(t):
+        pr = int(prefix_row[i])
+        if pr < -1:
+            continue
+        f = int(first_row[i])
+        kk, vv = k[f:i + 1].float()[:, heads], v[f:i + 1].float()[:, heads]        # [n, HQ, D]
+        s = torch.einsum("hd,nhd->hn", q[i].float(), kk) * (d ** -0.5)
+        own_lse = torch.logsumexp(s, dim=-1)
+        own = torch.einsum("hn,nhd->hd", torch.exp(s - own_lse.unsqueeze(-1)), vv)
+        if pr >= 0:
+            w = torch.sigmoid(pre_lse[pr].float() - own_lse).unsqueeze(-1)          # the prefix part's share
+            own = own + (pre[pr].float() - own) * w
+        out[i] = own
+    return out
 
 
 # --------------------------------------------------------------------------

@@ -241,3 +241,73 @@ def test_store_takes_wider_inputs_at_full_precision(dtype):
         assert torch.equal(words(kc[0]), ref_k[0])
         assert torch.equal(words(vc[0]), ref_v[0])
         assert torch.equal(vc[1].cpu(), ref_v[1])
+
+
+@pytest.mark.parametrize("hq,hkv,d,page,group,rows,prefixes", [
+    (32, 8, 128, 256, 64, 16, [700, 2100, 0, 33]),          # verify kernel, several splits, an empty prefix
+    (16, 8, 128, 128, 64, 16, [257, 1000]),                 # two heads per group: 32 rows per KV head
+    (4, 2, 64, 128, 32, 16, [300, 90]),                     # D = 64: the generic kernel
+    (8, 1, 128, 128, 128, 8, [513, 40, 1300]),              # eight heads per group: blocks of 8 rows
+])
+def test_prefix_attention_against_oracle(hq, hkv, d, page, group, rows, prefixes):
+    """The pool half of chunked prefill: out and log-sum-exp against the oracle on dequantised slots,
+    and merging it with an fp32 attention over extra keys equals attention over both."""
+    from linkq2_b200.kernels.kv4.ops import paged_attention_prefix
+    g = torch.Generator().manual_seed(hq + d)
+    blocks = [(n + page - 1) // page for n in prefixes]
+    n_blocks = sum(blocks) + 2
+    k, v = ok.seeded_kv(n_blocks * page, hkv, d, seed=d + rows, outlier_channels=2)
+    kc, vc = ok.empty_pool(n_blocks * page, hkv, d, group)
+    kc[1].copy_(ok.static_k_scale(k))
+    ok.store_kv_quant(k, v, kc, vc, torch.arange(n_blocks * page), v_group=group)
+    perm = torch.randperm(n_blocks, generator=g).tolist()
+    table = torch.full((len(prefixes), max(max(blocks), 1)), -1, dtype=torch.int32)
+    for i, nb in enumerate(blocks):
+        table[i, :nb] = torch.tensor(perm[:nb], dtype=torch.int32)
+        perm = perm[nb:]
+    lens = torch.tensor(prefixes, dtype=torch.int32)
+    q = (torch.randn(len(prefixes) * rows, hq, d, generator=g) * 0.7).half()
+    gk, gv = cuda_pool(kc, vc)
+    out, lse = paged_attention_prefix(q.cuda(), gk, gv, table.cuda(), lens.cuda(), block_n=page, num_kv_heads=hkv,
+                                      v_group=group, rows=rows)
+    ref, ref_lse = ok.paged_attention_prefix(q, kc, vc, table, lens, block_n=page, num_kv_heads=hkv,
+                                             v_group=group, rows=rows)
+    # fp16 outputs up to ~15 with the x10 channels: 2e-3 plus the output's own rounding
+    assert bool(((out.float().cpu() - ref).abs() <= ATOL + ref.abs() * 2.0 ** -11).all())
+    live = torch.isfinite(ref_lse)
+    assert torch.equal(torch.isfinite(lse.cpu()), live)
+    assert (lse.cpu()[live] - ref_lse[live]).abs().max().item() < 2e-3
+    assert (out.float().cpu()[~live] == 0).all()
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (16, 8, 128), (4, 2, 64), (8, 1, 128)])
+def test_chunk_attention_merges_own_rows_with_prefix_part(hq, hkv, d):
+    """A step of four sequences - 64 rows with a prefix part, 5 and 40 rows without, 7 rows that
+    the caller handles elsewhere - read through strided views of one fused buffer."""
+    from linkq2_b200.kernels.kv4.ops import chunk_attention
+    g = torch.Generator().manual_seed(hq * d)
+    counts = [64, 5, 40, 7]
+    t = sum(counts)
+    fused = (torch.randn(t, hq + 2 * hkv, d, generator=g) * 0.8).half()
+    fused[:, hq:hq + hkv, 3] *= 6                                   # an outlier channel in K
+    q, k, v = fused[:, :hq], fused[:, hq:hq + hkv], fused[:, hq + hkv:]
+    first, where, at = [], [], 0
+    for i, n in enumerate(counts):
+        first += [at] * n
+        where += list(range(n)) if i == 0 else [-1 if i < 3 else -2] * n
+        at += n
+    first, where = torch.tensor(first, dtype=torch.int32), torch.tensor(where, dtype=torch.int32)
+    pre = (torch.randn(64, hq, d, generator=g) * 0.5).half()
+    pre_lse = torch.randn(64, hq, generator=g) * 3 + 2
+    pre_lse[5] = float("-inf")                                       # an empty prefix part counts for nothing
+    pre_lse[9] = 40.0                                                # a dominant one takes the row over
+    gf = fused.cuda()
+    out = torch.full((t, hq, d), 7.0, dtype=torch.float16, device="cuda")
+    chunk_attention(gf[:, :hq], gf[:, hq:hq + hkv], gf[:, hq + hkv:], first.cuda(), where.cuda(), pre.cuda(),
+                    pre_lse.cuda(), out)
+    ref = ok.chunk_attention(q, k, v, first, where, pre, pre_lse)
+    got = out.float().cpu()
+    done = where >= -1
+    assert bool(((got[done] - ref[done]).abs() <= ATOL + ref[done].abs() * 2.0 ** -11).all())
+    assert bool((got[~done] == 7.0).all())                           # untouched rows
+    assert (got[9] - pre[9].float()).abs().max().item() < 1e-3

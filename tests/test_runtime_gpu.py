@@ -79,7 +79,9 @@ def make_runner(path, eager, drafts=0):
     model = build_from_checkpoint(path, device="cuda:0", max_position=512)
     rc = RunnerConfig(kvcache_block_size=128, num_kvcache_blocks=16, max_num_seqs=4, max_model_len=512,
                       enforce_eager=eager, spec_num_drafts=drafts)
-    return ModelRunner(model, rc, smooth_kv=amax_calibration(2, 1, 64, 0.3), device="cuda:0")
+    runner = ModelRunner(model, rc, smooth_kv=amax_calibration(2, 1, 64, 0.3), device="cuda:0")
+    runner.keep_logits = True
+    return runner
 
 
 def generate(runner, prompts, new_tokens, chunk):
@@ -124,6 +126,32 @@ def test_greedy_tokens_match_oracle(tmp_path, affine, eager, chunk):
         assert (logits[i] - expected).abs().max() / expected.pow(2).mean().sqrt() < 2e-2
     if not eager:
         assert runner.graph_replays == 63
+
+
+def test_temperature_rows_are_sampled_and_greedy_rows_are_not(tmp_path):
+    """Per-row temperatures as in the reference's sampler (``execute/sampler.py:8-13``): a row
+    at temperature 0 keeps the arg-max, a hot row is drawn from the softmax; the same seed
+    draws the same tokens again; and without ``keep_logits`` the greedy path leaves no logits."""
+    write_checkpoint(tmp_path / "w4")
+    g = torch.Generator().manual_seed(8)
+    prompt = torch.randint(0, 127, (20,), generator=g).tolist()
+    runner = make_runner(tmp_path / "w4", eager=True)
+    (greedy, _), _ = generate(runner, [prompt, prompt], 24, 1000)
+
+    def sampled(seed):
+        runner.temperature = torch.tensor([0.0, 200.0], device="cuda:0")
+        runner.sample_generator = torch.Generator(device="cuda:0").manual_seed(seed)
+        out, _ = generate(runner, [prompt, prompt], 24, 1000)
+        runner.temperature = 0.0
+        return out
+
+    first, again = sampled(11), sampled(11)
+    assert first[0] == greedy                       # the cold row
+    assert first[1] != greedy and len(set(first[1])) > 8
+    assert first == again
+    runner.keep_logits = False
+    (plain, _), _ = generate(runner, [prompt, prompt], 24, 1000)
+    assert plain == greedy and runner.last_logits is None
 
 
 def test_verify_rows_match_sequential_decode(tmp_path):
@@ -261,6 +289,7 @@ def test_qwen3_1p7b_width_batch1_matches_oracle(tmp_path):
     shape = (4, 8, 128)
     runner = ModelRunner(model, rc, smooth_kv={"lambda": torch.ones(shape), "kscale": torch.full(shape, 0.5)},
                          device="cuda:0")
+    runner.keep_logits = True
     g = torch.Generator().manual_seed(2)
     prompt = torch.randint(0, 4095, (48,), generator=g).tolist()
     seq = Sequence(prompt, 256)

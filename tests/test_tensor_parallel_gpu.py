@@ -35,7 +35,14 @@ def _worker(rank, world, port, ckpt, prompts, eager, results):
     rc = RunnerConfig(kvcache_block_size=128, num_kvcache_blocks=16, max_num_seqs=4, max_model_len=512,
                       enforce_eager=eager, spec_num_drafts=0)
     runner = ModelRunner(model, rc, smooth_kv=amax_calibration(2, HKV, 64, 0.3), device=device)
+    runner.keep_logits = True
     tokens, _ = generate(runner, prompts, NEW_TOKENS, 16)
+    # the pair exchange of the greedy path against the arg-max of the gathered logits, ties included
+    g = torch.Generator(device=device).manual_seed(3)
+    h = torch.randn(6, model.config.hidden_size, generator=g, device=device).half()
+    h[4] = 0                                    # every logit equal: the lowest index must win
+    h[5] = h[3]
+    assert torch.equal(model.greedy_tokens(h), model.compute_logits(h).argmax(dim=-1))
     results[rank] = (tokens, runner.last_logits.float().cpu(), runner.graph_replays, tp.size)
     runner.shutdown()                       # graphs hold NCCL kernels: release them before the group
     parallel.shutdown()

@@ -646,8 +646,9 @@ def run_case(args):
     torch.cuda.set_device(0)
     g = torch.Generator().manual_seed(0)
     peaks, which = measured_peaks()
-    if args.case in ("w4a16_gemv", "w4a16_m32"):
-        k, n, m, copies = 4096, 24576, (1 if args.case == "w4a16_gemv" else 32), 4
+    flops = None
+    if args.case in ("w4a16_gemv", "w4a16_m32", "w4a16_m512"):
+        k, n, m, copies = 4096, 24576, {"w4a16_gemv": 1, "w4a16_m32": 32, "w4a16_m512": 512}[args.case], 4
         vals = (torch.randint(0, 16, (n, k), generator=g, dtype=torch.uint8).to(torch.int16) - 8).to(torch.int8)
         scale = (torch.rand(n, k // 128, generator=g) * 0.01 + 0.001).half()
         layers = [make_quant_linear("b200", vals, scale, group_size=128, symmetric=True, device="cuda",
@@ -657,7 +658,27 @@ def run_case(args):
         set_constant_weights(True)                     # as the runtime does once the checkpoint is loaded
         calls = [lambda l=l: l(x) for l in layers]
         nbytes = k * n // 2 + 2 * (k // 128) * n + 2 * m * (k + n)
+        flops = 2.0 * m * k * n if m >= 256 else None          # tensor-bound from a few hundred rows on
         what = f"gate_up geometry K={k} N={n} M={m}, {copies} distinct weight copies"
+    elif args.case == "kv4_verify":
+        hq, hkv, d, page, bs, ctx, mrows = 32, 8, 128, 256, 32, 2200, 16
+        nb = bs * ((ctx + mrows + page - 1) // page)
+        slots = nb * page
+        kq = torch.randint(-2**31, 2**31 - 1, (slots, hkv, d // 8), dtype=torch.int32, device="cuda")
+        vq = torch.randint(-2**31, 2**31 - 1, (slots, hkv, d // 8), dtype=torch.int32, device="cuda")
+        ks = (torch.rand(hkv, d, device="cuda") * 0.1 + 0.05).half()
+        vs = (torch.rand(slots, hkv, 2, device="cuda") * 0.1 + 0.05).half()
+        table = torch.randperm(nb, generator=g).int().view(bs, -1).cuda()
+        q = (torch.randn(bs * mrows, hq, d, device="cuda") * 0.5).half()
+        lens = torch.full((bs,), ctx, dtype=torch.int32, device="cuda")
+        calls = [lambda: paged_attention_decode(q, (kq, ks), (vq, vs), table, lens, block_n=page,
+                                                num_kv_heads=hkv, verify_m=mrows)] * 3
+        nbytes = bs * (ctx + mrows - 1) * hkv * (d + 2 * (d // 64)) + 4 * bs * mrows * hq * d
+        # QK^T and PV over the cached tokens, 64 query rows per KV head, without the second pass that the
+        # fp16-split queries add to QK^T
+        flops = 4.0 * bs * hq * mrows * (ctx + mrows - 1) * d
+        what = (f"verify: batch {bs}, context {ctx}, {mrows} positions, Qwen3-8B heads, page {page}, v_group 64 "
+                f"({bs * ctx * hkv * 132 // 2**20} MB of cache; bound by the warp-level tensor op, see achieved_tflops)")
     else:
         hq, hkv, d, page, bs, ctx = 32, 8, 128, 256, 64, 4096
         nb = bs * (ctx // page)
@@ -695,10 +716,13 @@ def run_case(args):
             times.append(a.elapsed_time(b))
     us = sorted(times)[len(times) // 2] * 1e3 / len(calls)
     gbs = nbytes / us / 1e3
-    print(json.dumps({"case": args.case, "workload": what, "launches_timed": len(calls), "replays": "median of 5",
-                      "us_per_launch": round(us, 2), "algorithmic_bytes_per_launch": nbytes,
-                      "achieved_gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 4), "of": which}),
-          flush=True)
+    line = {"case": args.case, "workload": what, "launches_timed": len(calls), "replays": "median of 5",
+            "us_per_launch": round(us, 2), "algorithmic_bytes_per_launch": nbytes,
+            "achieved_gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 4), "of": which}
+    if flops is not None:
+        line["achieved_tflops"] = round(flops / us / 1e6, 1)
+        line["frac_of_bf16_burst"] = round(flops / us / 1e6 / peaks["bf16_tflops"], 4)
+    print(json.dumps(line), flush=True)
 
 
 def main():
@@ -714,7 +738,7 @@ def main():
                     help="qwen3_8b: the workload of the metric (configs[4]); qwen3_1p7b: configs[3], batch-1 decode")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the timed decode steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
-    ap.add_argument("--case", default=None, choices=["w4a16_gemv", "w4a16_m32", "kv4_decode"],
+    ap.add_argument("--case", default=None, choices=["w4a16_gemv", "w4a16_m32", "w4a16_m512", "kv4_decode", "kv4_verify"],
                     help="run one small single-kernel case instead of the workload (the profiled cases)")
     args = ap.parse_args()
     if args.case:

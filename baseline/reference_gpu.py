@@ -203,6 +203,34 @@ def ours_generate(quantized, kscale, kw, prompt, new_tokens, max_len):
     return tokens, dt / max(new_tokens - 1, 1) * 1e3, first_logits, last_logits
 
 
+def ours_follow(quantized, kscale, kw, prompt, forced, max_len):
+    """This library's runtime fed with the reference's tokens (teacher forcing): at every step the
+    margin, in units of the logits' RMS, by which this runtime's top logit exceeds its logit of the
+    token the reference chose (0 where both choose the same token)."""
+    import torch
+    from linkq2_b200.runtime.execute.model_runner import ModelRunner, RunnerConfig
+    from linkq2_b200.runtime.quantization import build_from_checkpoint
+    from linkq2_b200.runtime.state import BlockPool, Sequence
+    model = build_from_checkpoint(quantized, device="cuda:0", max_position=max_len + 64)
+    blocks = (max_len + 255) // 256 + 1
+    rc = RunnerConfig(kvcache_block_size=256, num_kvcache_blocks=blocks, max_num_seqs=1, max_model_len=max_len,
+                      enforce_eager=False)
+    shape = (kw["num_hidden_layers"], kw["num_key_value_heads"], kw["head_dim"])
+    runner = ModelRunner(model, rc, smooth_kv={"lambda": torch.ones(shape), "kscale": torch.full(shape, kscale)},
+                         device="cuda:0")
+    runner.keep_logits = True
+    seq = Sequence(list(prompt), 256)
+    BlockPool(blocks).ensure(seq, len(prompt) + len(forced) + 8)
+    margins = []
+    for i, token in enumerate(forced):
+        runner.run([seq], i == 0)
+        logits = runner.last_logits.float()[-1]
+        margins.append(float((logits.max() - logits[token]) / logits.pow(2).mean().sqrt()))
+        seq.append(token)
+    runner.shutdown()
+    return margins
+
+
 def section_tokens(args):
     import tempfile
     import torch
@@ -231,6 +259,13 @@ def section_tokens(args):
                     rec.update(reference_tokens=ref[:64], reference_tpot_ms=round(ref_ms, 3),
                                identical_prefix=same, first_64_identical=bool(same >= min(64, n)),
                                all_identical=bool(ref[:n] == ours[:n]))
+                    if same < n:
+                        # random-init logits are nearly flat, so one near-tie sends two correct runs apart;
+                        # follow the reference's tokens and measure every disagreement
+                        margins = ours_follow(quantized, 0.5, kw, prompt, ref[:64], max_len)
+                        off = [m for m in margins if m > 0]
+                        rec.update(forced_steps=len(margins), forced_disagreements=len(off),
+                                   forced_max_margin_over_rms=round(max(off), 5) if off else 0.0)
                     if ref_logits:
                         a, b = ref_logits[0][-1], ours_first[-1]
                         rec["first_logits_err_over_rms"] = round(float((a - b).abs().max() / b.pow(2).mean().sqrt()), 5)

@@ -50,7 +50,8 @@ constexpr int kUM = 128;          // output channels per CTA (MMA M)
 // k per pipeline stage: 128 for batch tiles up to 64 rows (half as many barrier rounds per
 // byte as 64, measured 8-15 % faster), 64 beyond, where the activation tile of a stage grows
 __host__ __device__ constexpr int stage_k(int mb) { return mb <= 64 ? 128 : 64; }
-constexpr int kUThreads = 320;    // 10 warps
+constexpr int kUThreads = 352;    // 11 warps: TMA producer, MMA issuer, 8 dequantisers, second MMA issuer
+constexpr int kIssuer2 = 10;      // warp index of the second issuer
 constexpr int kDequantThreads = 256;
 
 struct UParams {
@@ -167,9 +168,9 @@ __host__ __device__ constexpr uint32_t umma_idesc(int mma_m, int mma_n) {
 template <int MB, int GPSU>
 struct ULayout {
     static constexpr int UK = stage_k(MB);
-    // A tiles in tensor memory.  A 128-k tile takes 64 columns; one of them plus the accumulator
-    // fits the 128-column allocation that lets four CTAs share an SM, and the MMAs of a stage
-    // are short enough that the next stage's conversion (in registers) hides them.
+    // A tiles in tensor memory.  A 128-k tile takes 64 columns; one of them plus the two accumulators
+    // of a 32-row batch fits a 128-column allocation, so three CTAs share an SM.  (Two A tiles with two
+    // CTAs per SM were measured and are no faster: 2.8 against 2.6 stages per microsecond and SM.)
     static constexpr int A_STAGES = UK == 128 ? 1 : 3;
     static constexpr int A_COLS = UK / 2;                           // 32-bit TMEM columns per A tile (two fp16 each)
     static constexpr int XBOX_BYTES = (MB * 128 + 1023) / 1024 * 1024;   // [MB m][64 k] fp16, swizzled
@@ -190,10 +191,15 @@ struct ULayout {
     static constexpr bool PUSH = MB <= 64;
     static constexpr int RECV_OFF = RING_BYTES;
     static constexpr int DATA_BYTES = PUSH ? RING_BYTES + RED_BYTES : (RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES);
-    static constexpr int NBARS = 2 * R_STAGES + 2 * A_STAGES + 1;
+    static constexpr int NBARS = 2 * R_STAGES + (1 + (UK == 128 ? 2 : 1)) * A_STAGES + 1;
     static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + NBARS * 8 + 16;
     static constexpr int ACC_COLS = MB < 32 ? 32 : MB;
-    static constexpr int TMEM_NEED = ACC_COLS + A_STAGES * A_COLS;
+    // One thread issues a tcgen05.mma of this size about every 115 cycles, whatever the tensor pipe is
+    // doing, and with a single A tile the stage's MMAs sit between "tile written" and "tile free" on the
+    // CTA's critical path.  With 128-k stages two warps therefore issue half of a stage's MMAs each, into
+    // accumulators of their own (their rates add up); the epilogue sums the two.
+    static constexpr int ISS = UK == 128 ? 2 : 1;
+    static constexpr int TMEM_NEED = ISS * ACC_COLS + A_STAGES * A_COLS;
     static constexpr int TMEM_COLS = TMEM_NEED <= 64 ? 64 : (TMEM_NEED <= 128 ? 128 : (TMEM_NEED <= 256 ? 256 : 512));
     static_assert(TMEM_NEED <= 512, "tensor memory has 512 columns");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
@@ -212,14 +218,15 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     using L = ULayout<MB, GPSU>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    constexpr int RS = L::R_STAGES, AS = L::A_STAGES, UK = L::UK;
+    constexpr int RS = L::R_STAGES, AS = L::A_STAGES, UK = L::UK, ISS = L::ISS;
     const uint32_t bars = smem_u32(smem + L::DATA_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::DATA_BYTES + L::NBARS * 8);
     auto raw_full = [&](int s) { return bars + 8 * s; };               // TMA bytes of raw stage s landed
     auto raw_free = [&](int s) { return bars + 8 * (RS + s); };        // MMAs that read its activations are done
-    auto a_full = [&](int s) { return bars + 8 * (2 * RS + s); };      // A tile s written by all dequant warps
-    auto a_free = [&](int s) { return bars + 8 * (2 * RS + AS + s); }; // MMAs that read A tile s are done
-    const uint32_t acc_full = bars + 8 * (2 * RS + 2 * AS);
+    // k-half h of A tile s written by the dequant warps that own it (all of them when there is one issuer)
+    auto a_full = [&](int s, int h) { return bars + 8 * (2 * RS + ISS * s + h); };
+    auto a_free = [&](int s) { return bars + 8 * (2 * RS + ISS * AS + s); };   // MMAs that read A tile s are done
+    const uint32_t acc_full = bars + 8 * (2 * RS + (ISS + 1) * AS);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile_n0 = blockIdx.x * kUM;
@@ -234,13 +241,13 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     if (tid == 0) {
         for (int i = 0; i < RS; ++i) {
             mbar_init(raw_full(i), 1);
-            mbar_init(raw_free(i), 1);
+            mbar_init(raw_free(i), ISS);
         }
         for (int i = 0; i < AS; ++i) {
-            mbar_init(a_full(i), kDequantThreads / 32);
-            mbar_init(a_free(i), 1);
+            for (int h = 0; h < ISS; ++h) mbar_init(a_full(i, h), kDequantThreads / 32 / ISS);
+            mbar_init(a_free(i), ISS);
         }
-        mbar_init(acc_full, 1);
+        mbar_init(acc_full, ISS);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     if (warp == 1) {
@@ -297,29 +304,32 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             }
             __syncwarp();
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || (ISS == 2 && warp == kIssuer2)) {
+        // ------------------------------------------------------------ MMA issuer(s)
         pdl_wait();
+        const int half = warp == 1 ? 0 : 1;                   // which k-half of every stage, and which accumulator
+        constexpr int KSTEPS = UK / 16 / ISS;
         constexpr uint32_t idesc = umma_idesc(kUM, MB);
-        constexpr int U = AS == 1 ? RS : 1;                   // unrolled over the raw ring, as the dequantisers are
+        constexpr int U = RS % AS == 0 && UK == 128 ? RS : 1;   // unrolled over the raw ring, as the dequantisers are
         for (int it0 = 0; it0 < my_stages; it0 += U) {
 #pragma unroll
           for (int us = 0; us < U; ++us) {
             const int it = it0 + us;
             if (it >= my_stages) break;
-            const int rslot = U == 1 ? it % RS : us, aslot = it % AS;
-            mbar_wait_bounded(a_full(aslot), (it / AS) & 1);
+            const int rslot = U == 1 ? it % RS : us, aslot = U == 1 ? it % AS : us % AS;
+            mbar_wait_bounded(a_full(aslot, half), (it / AS) & 1);
             tc_fence_after();
             if (lane == 0) {
-                const uint32_t a_tmem = tmem_base + L::ACC_COLS + aslot * L::A_COLS;
+                const uint32_t a_tmem = tmem_base + ISS * L::ACC_COLS + aslot * L::A_COLS;
                 const uint32_t xbase = smem_u32(r_ring + rslot * L::R_STAGE_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < UK / 16; ++kk) {
+                for (int ks = 0; ks < KSTEPS; ++ks) {
                     // a K step of 16 fp16: 8 TMEM columns of A, 32 bytes inside the swizzled rows of B
                     // (a 64-k box holds four such steps)
-                    umma_f16_ts(tmem_base, a_tmem + kk * 8,
+                    const int kk = half * KSTEPS + ks;
+                    umma_f16_ts(tmem_base + half * L::ACC_COLS, a_tmem + kk * 8,
                                 smem_desc_sw128(xbase + (kk >> 2) * L::XBOX_BYTES + (kk & 3) * 32), idesc,
-                                (it > 0 || kk > 0) ? 1u : 0u);
+                                (it > 0 || ks > 0) ? 1u : 0u);
                 }
                 umma_commit(a_free(aslot));                   // both buffers are reusable once these MMAs are done
                 umma_commit(raw_free(rslot));
@@ -328,7 +338,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             __syncwarp();
           }
         }
-    } else {
+    } else if (warp < 2 + kDequantThreads / 32) {
         // ------------------------------------------------------------ dequantise
         pdl_wait();
         // A warp reaches the 32 TMEM lanes of its quarter (warp % 4); lane = output channel.  Two
@@ -345,18 +355,18 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(a_full(it_done % AS));
+            if (lane == 0) mbar_arrive(a_full(it_done % AS, ISS == 2 ? khalf : 0));
         };
         // With a single A tile the loop is unrolled over the raw ring, which makes the stage
         // slot, its shared-memory addresses and its barrier compile-time constants.
-        constexpr int U = AS == 1 ? RS : 1;
+        constexpr int U = RS % AS == 0 && UK == 128 ? RS : 1;
         uint32_t ring_phase = 0;                              // (it / RS) & 1 when U == RS
         for (int it0 = 0; it0 < my_stages; it0 += U, ring_phase ^= 1u) {
 #pragma unroll
           for (int us = 0; us < U; ++us) {
             const int it = it0 + us;
             if (it >= my_stages) break;
-            const int rslot = U == 1 ? it % RS : us, aslot = it % AS;
+            const int rslot = U == 1 ? it % RS : us, aslot = U == 1 ? it % AS : us % AS;
             const unsigned char* rbase = r_ring + rslot * L::R_STAGE_BYTES;
             mbar_wait_bounded(raw_full(rslot), U == 1 ? uint32_t(it / RS) & 1u : ring_phase);
             const uint32_t* raw = reinterpret_cast<const uint32_t*>(rbase + L::RAW_OFF);
@@ -398,7 +408,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                     cols[4 * r4 + 2] = __byte_perm(v04, v15, 0x7632);        // k4 k5
                     cols[4 * r4 + 3] = __byte_perm(v26, v37, 0x7632);        // k6 k7
                 }
-                tmem_st16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + aslot * L::A_COLS +
+                tmem_st16(tmem_base + (uint32_t(quarter * 32) << 16) + ISS * L::ACC_COLS + aslot * L::A_COLS +
                               khalf * (UK / 4) + 16 * b, cols);
             }
           }
@@ -433,6 +443,12 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                 float v[16];
                 if (my_stages > 0) {
                     tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + c0, v);
+                    if (ISS == 2) {
+                        float v2[16];
+                        tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + c0, v2);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[i] += v2[i];
+                    }
                 } else {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) v[i] = 0.f;
@@ -512,6 +528,12 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                 float v[16];
                 if (my_stages > 0) {
                     tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + c0, v);
+                    if (ISS == 2) {
+                        float v2[16];
+                        tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + c0, v2);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[i] += v2[i];
+                    }
                 } else {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) v[i] = 0.f;

@@ -134,6 +134,24 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]) : "memory");
 }
+// 16 consecutive accumulator columns of this thread's TMEM lane from each of two accumulators, summed
+// (one wait for both loads)
+__device__ __forceinline__ void tmem_ld16_sum2(uint32_t taddr_a, uint32_t taddr_b, float (&v)[16]) {
+    uint32_t r[16], q[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr_a) : "memory");
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]), "=r"(q[7]),
+          "=r"(q[8]), "=r"(q[9]), "=r"(q[10]), "=r"(q[11]), "=r"(q[12]), "=r"(q[13]), "=r"(q[14]), "=r"(q[15])
+        : "r"(taddr_b) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]) + __uint_as_float(q[i]);
+}
 // 16 consecutive accumulator columns of this thread's TMEM lane
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
@@ -442,13 +460,8 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             for (int c0 = 0; c0 < MB; c0 += 16) {
                 float v[16];
                 if (my_stages > 0) {
-                    tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + c0, v);
-                    if (ISS == 2) {
-                        float v2[16];
-                        tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + c0, v2);
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) v[i] += v2[i];
-                    }
+                    const uint32_t acc = tmem_base + (uint32_t(quarter * 32) << 16) + c0;
+                    if (ISS == 2) tmem_ld16_sum2(acc, acc + L::ACC_COLS, v); else tmem_ld16(acc, v);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) v[i] = 0.f;
@@ -527,13 +540,8 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             for (int c0 = 0; c0 < MB; c0 += 16) {
                 float v[16];
                 if (my_stages > 0) {
-                    tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + c0, v);
-                    if (ISS == 2) {
-                        float v2[16];
-                        tmem_ld16(tmem_base + (uint32_t(quarter * 32) << 16) + L::ACC_COLS + c0, v2);
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) v[i] += v2[i];
-                    }
+                    const uint32_t acc = tmem_base + (uint32_t(quarter * 32) << 16) + c0;
+                    if (ISS == 2) tmem_ld16_sum2(acc, acc + L::ACC_COLS, v); else tmem_ld16(acc, v);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) v[i] = 0.f;

@@ -3,7 +3,9 @@
 Drop-in for ``GemLiteLinear`` (``qslab/runtime/backends/gemlite.py:8-43``): same
 constructor contract, same buffer names, shapes and dtypes (``packed [K/8, N]
 int32``, ``scales [K/G, N] fp16``, ``zeros`` 0-dim int32 8 or ``[K/G, N] fp16``,
-``input_scale [K]`` or ``None``), same exceptions."""
+``input_scale [K]`` or ``None``), same exceptions - with one gap: the reference's
+constructor also takes bf16 activations (``gemlite.py:14``), these kernels compute in fp16
+only, as the reference's runtime does (``model_runner.py:33``), and bf16 raises ``TypeError``."""
 import torch
 
 from linkq2_b200.kernels.gemlite.bitpack import pack_w4

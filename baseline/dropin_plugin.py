@@ -1,5 +1,5 @@
 """pytest plugin that performs, at run time, the rebinding a maintainer of the reference
-would commit to use this library (the two edits INTEGRATION.md shows), so that the
+would commit to use this library (a backend registration and three rebound names), so that the
 reference's own, unmodified tests exercise the sm_100a kernels:
 
   * ``qslab.runtime.backends``: ``'b200'`` joins ``QUANT_BACKENDS`` and

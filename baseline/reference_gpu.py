@@ -8,7 +8,8 @@
     python baseline/reference_gpu.py kernels   # device time of the reference's Triton kernels and of this library's
     python baseline/reference_gpu.py all
 
-Every section prints one JSON line and appends it to ``gpurun_out/reference_gpu.jsonl``; a section
+Every section prints one JSON line and appends it to ``reference_gpu.jsonl`` in the output directory
+(``--out``, default ``baseline/out``, or the environment variable ``LINKQ2_REFERENCE_OUT``); a section
 that cannot run records the error text instead (that text is then the result).  Nothing here is
 imported by the package, the tests or ``bench.py``.
 """
@@ -28,11 +29,11 @@ ROOT = HERE.parent
 for p in (str(HERE / "_ref"), str(ROOT)):
     if p not in sys.path:
         sys.path.insert(0, p)
-OUT = ROOT / "gpurun_out"
+OUT = Path(os.environ.get("LINKQ2_REFERENCE_OUT", HERE / "out"))
 
 
 def emit(section: str, payload: dict) -> None:
-    OUT.mkdir(exist_ok=True)
+    OUT.mkdir(parents=True, exist_ok=True)
     line = json.dumps({"section": section, **payload})
     print(line, flush=True)
     with open(OUT / "reference_gpu.jsonl", "a") as f:
@@ -70,7 +71,7 @@ def run_pytest(env_extra: dict, tag: str) -> dict:
 
 
 def section_tests(_args):
-    OUT.mkdir(exist_ok=True)
+    OUT.mkdir(parents=True, exist_ok=True)
     stock = run_pytest({}, "stock")
     emit("tests.stock", {"what": "reference tests, reference kernels, image as is", **stock})
     compat = run_pytest({"LINKQ2_HF_COMPAT": "1"}, "stock_hf_compat")
@@ -446,7 +447,11 @@ def main():
     ap.add_argument("section", choices=["tests", "tokens", "store", "kernels", "all"])
     ap.add_argument("--layers", type=int, default=None, help="decoder layers of the 1.7B-geometry checkpoint (default 28)")
     ap.add_argument("--only", default=None, help="tokens: run this geometry only")
+    ap.add_argument("--out", default=None, help="directory for reference_gpu.jsonl and the test logs")
     args = ap.parse_args()
+    if args.out:
+        global OUT
+        OUT = Path(args.out)
     if not (HERE / "_ref" / "qslab").exists():
         emit(args.section, {"error": "baseline/_ref is missing: run baseline/install_reference.sh first"})
         return

@@ -50,7 +50,7 @@ constexpr int kUM = 128;          // output channels per CTA (MMA M)
 // k per pipeline stage: 128 for batch tiles up to 64 rows (half as many barrier rounds per
 // byte as 64, measured 8-15 % faster), 64 beyond, where the activation tile of a stage grows
 __host__ __device__ constexpr int stage_k(int mb) { return mb <= 64 ? 128 : 64; }
-constexpr int kUThreads = 352;    // 11 warps: TMA producer, MMA issuer, 8 dequantisers, second MMA issuer
+constexpr int kUThreads = 320;    // 10 warps: TMA producer, MMA issuer, 8 dequantisers (+ one more issuer, see ISS)
 constexpr int kIssuer2 = 10;      // warp index of the second issuer
 constexpr int kDequantThreads = 256;
 
@@ -217,6 +217,7 @@ struct ULayout {
     // CTA's critical path.  With 128-k stages two warps therefore issue half of a stage's MMAs each, into
     // accumulators of their own (their rates add up); the epilogue sums the two.
     static constexpr int ISS = UK == 128 ? 2 : 1;
+    static constexpr int THREADS = kUThreads + 32 * (ISS - 1);
     static constexpr int TMEM_NEED = ISS * ACC_COLS + A_STAGES * A_COLS;
     static constexpr int TMEM_COLS = TMEM_NEED <= 64 ? 64 : (TMEM_NEED <= 128 ? 128 : (TMEM_NEED <= 256 ? 256 : 512));
     static_assert(TMEM_NEED <= 512, "tensor memory has 512 columns");
@@ -229,7 +230,7 @@ struct ULayout {
 __host__ __device__ constexpr int resident_ctas(int mb) { return mb <= 32 ? 3 : (mb <= 128 ? 2 : 1); }
 
 template <int MB, bool ZTABLE, int GPSU>
-__global__ void __launch_bounds__(kUThreads, resident_ctas(MB))
+__global__ void __launch_bounds__((ULayout<MB, GPSU>::THREADS), resident_ctas(MB))
 w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                   const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                   const UParams p) {
@@ -487,7 +488,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
         };
         if (p.silu) {
             const int octs = W / 8;                        // [4 gate | 4 up] blocks of my slice
-            for (int e = tid; e < rows * octs; e += kUThreads) {
+            for (int e = tid; e < rows * octs; e += L::THREADS) {
                 const int ml = e / octs, col = (e - ml * octs) * 8;
                 const int nn = tile_n0 + rank * W + col;
                 if (nn < p.n)
@@ -512,7 +513,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                      (size_t(seq & 1u) * world + me) * 2 * p.push.max_bytes;
             }
             const int quads = W / 4;
-            for (int e = tid; e < rows * quads; e += kUThreads) {
+            for (int e = tid; e < rows * quads; e += L::THREADS) {
                 const int ml = e / quads, col = (e - ml * quads) * 4;
                 const float4 sum = slice_sum(ml, col);
                 const int nn = tile_n0 + rank * W + col;
@@ -569,7 +570,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             };
             if (p.silu) {                                  // q0 is even for every power-of-two cluster size
                 const int octs = quads / 2;
-                for (int e = tid; e < rows * octs; e += kUThreads) {
+                for (int e = tid; e < rows * octs; e += L::THREADS) {
                     const int ml = e / octs, col = (q0 + 2 * (e % octs)) * 4;
                     const int nn = tile_n0 + col;
                     if (nn < p.n)
@@ -577,7 +578,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
                             silu_mul_quad(tile_sum(ml, col), tile_sum(ml, col + 4));
                 }
             } else {
-                for (int e = tid; e < rows * quads; e += kUThreads) {
+                for (int e = tid; e < rows * quads; e += L::THREADS) {
                     const int ml = e / quads, col = (q0 + e % quads) * 4;
                     const float4 sum = tile_sum(ml, col);
                     const int nn = tile_n0 + col;
@@ -676,7 +677,7 @@ int launch_umma(const __half* x, int64_t ldx, const int32_t* packed, const __hal
     const int ctas = pl.n_tiles * pl.ranks * pl.m_tiles;
     const int per_sm = cdiv(ctas, kNumSMs);
     if (per_sm < resident_ctas(MB)) smem = std::max(smem, size_t(kMaxSmemPerCta / per_sm - 1024));
-    return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(kUThreads), smem, st, pl.ranks,
+    return launch_pdl(kernel, dim3(pl.n_tiles, pl.ranks, pl.m_tiles), dim3(L::THREADS), smem, st, pl.ranks,
                       map_w, map_x, map_s, map_z, p);
 }
 

@@ -512,38 +512,6 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
         }
     }
 
-    // ---- Q' = q * ks of all rows, high and low parts, stored order
-    if (!idle) {
-        const __half* ksp = p.ks + kvh * D;
-        for (int idx = tid; idx < ROWS * NW; idx += kThreads) {
-            const int row = idx / NW, c8 = idx % NW;
-            __half hi[8], lo[8];
-            if (row < rows_valid) {
-                const __half* qp = p.q + int64_t(seq * p.m + row / rep) * p.q_stride + (kvh * rep + row % rep) * D + 8 * c8;
-                __half qraw[8], sraw[8];
-                *reinterpret_cast<uint4*>(sraw) = *reinterpret_cast<const uint4*>(ksp + 8 * c8);
-                if ((reinterpret_cast<uintptr_t>(qp) & 15) == 0) {
-                    *reinterpret_cast<uint4*>(qraw) = *reinterpret_cast<const uint4*>(qp);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) qraw[i] = qp[i];
-                }
-#pragma unroll
-                for (int ps = 0; ps < 8; ++ps) {             // stored position ps holds natural channel ps/2 + 4 (ps%2)
-                    const int i = (ps >> 1) + 4 * (ps & 1);
-                    const float v = __half2float(qraw[i]) * __half2float(sraw[i]);      // exact in fp32
-                    hi[ps] = __float2half_rn(v);
-                    lo[ps] = __float2half_rn(v - __half2float(hi[ps]));
-                }
-            } else {
-#pragma unroll
-                for (int ps = 0; ps < 8; ++ps) hi[ps] = lo[ps] = __float2half_rn(0.f);
-            }
-            *reinterpret_cast<uint4*>(sm_qh + row * kVStride + 8 * c8) = *reinterpret_cast<const uint4*>(hi);
-            *reinterpret_cast<uint4*>(sm_ql + row * kVStride + 8 * c8) = *reinterpret_cast<const uint4*>(lo);
-        }
-    }
-
     const bool mma_warp = warp < RT;
     const int r_lo = 16 * warp + g, r_hi = r_lo + 8;
     const bool v_lo = mma_warp && r_lo < rows_valid, v_hi = mma_warp && r_hi < rows_valid;
@@ -735,6 +703,39 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
     fetch(tile_begin, table_entry(tile_begin), kw[0], vw[0], vsc[0], live[0]);
     fetch(tile_begin + 1, table_entry(tile_begin + 1), kw[1], vw[1], vsc[1], live[1]);
     raw_ahead = table_entry(tile_begin + 2);
+    // the first two tiles are on their way while the queries are prepared
+    // ---- Q' = q * ks of all rows, high and low parts, stored order
+    if (!idle) {
+        const __half* ksp = p.ks + kvh * D;
+        for (int idx = tid; idx < ROWS * NW; idx += kThreads) {
+            const int row = idx / NW, c8 = idx % NW;
+            __half hi[8], lo[8];
+            if (row < rows_valid) {
+                const __half* qp = p.q + int64_t(seq * p.m + row / rep) * p.q_stride + (kvh * rep + row % rep) * D + 8 * c8;
+                __half qraw[8], sraw[8];
+                *reinterpret_cast<uint4*>(sraw) = *reinterpret_cast<const uint4*>(ksp + 8 * c8);
+                if ((reinterpret_cast<uintptr_t>(qp) & 15) == 0) {
+                    *reinterpret_cast<uint4*>(qraw) = *reinterpret_cast<const uint4*>(qp);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) qraw[i] = qp[i];
+                }
+#pragma unroll
+                for (int ps = 0; ps < 8; ++ps) {             // stored position ps holds natural channel ps/2 + 4 (ps%2)
+                    const int i = (ps >> 1) + 4 * (ps & 1);
+                    const float v = __half2float(qraw[i]) * __half2float(sraw[i]);      // exact in fp32
+                    hi[ps] = __float2half_rn(v);
+                    lo[ps] = __float2half_rn(v - __half2float(hi[ps]));
+                }
+            } else {
+#pragma unroll
+                for (int ps = 0; ps < 8; ++ps) hi[ps] = lo[ps] = __float2half_rn(0.f);
+            }
+            *reinterpret_cast<uint4*>(sm_qh + row * kVStride + 8 * c8) = *reinterpret_cast<const uint4*>(hi);
+            *reinterpret_cast<uint4*>(sm_ql + row * kVStride + 8 * c8) = *reinterpret_cast<const uint4*>(lo);
+        }
+    }
+
     if (live[0]) convert(0, kw[0], vw[0], vsc[0]);
     __syncthreads();                                              // Q' and the first tile are in place
     for (int tile = tile_begin; tile < tile_end; tile += 2) {
@@ -881,14 +882,14 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
     const int first = tile_begin + ws;
     const int n_my = first < tile_end ? (tile_end - first + wt - 1) / wt : 0;
 
-    // ---- Q'^T fragments (B operand), column n = g; lane t covers words 4t..4t+3.
-    // Q' = q * ks is exact in fp32 and is carried as a high and a low fp16 part: rounded to one fp16 it
-    // would shift every score of the row by the same channel-wise error, which does not average out over
-    // the tokens.
+    // Order of the prologue: the query and K-scale words are requested first (a few hundred bytes), then
+    // the ring is started (block-table read, copies: the whole grid's first stages are ~19 MB, about 3 us of
+    // HBM time), and the Q' fragments are computed from the words while those copies are in flight.  With
+    // the ring started after the Q' set-up the two phases were serial; with the query loads behind the
+    // copies they queue up behind 19 MB.
     const int qrow = PAIR ? (g >> 1) : g;
     const bool row_ok = qrow < rows_valid;
-    uint32_t qb[KWT][2][2], ql[PAIR ? 1 : KWT][2][2];
-    float qsum = 0.f;
+    uint4 q_words[KWT], s_words[KWT];
     {
         const int mrow = row_ok ? qrow / rep : 0;
         const __half* qp = p.q + int64_t(seq * p.m + mrow) * p.q_stride + (kvh * rep + (row_ok ? qrow % rep : 0)) * D;
@@ -897,72 +898,17 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
 #pragma unroll
         for (int wi = 0; wi < KWT; ++wi) {
             const int d0 = 8 * (t * KWT + wi);
-            __half qraw[8], sraw[8];
-            *reinterpret_cast<uint4*>(sraw) = *reinterpret_cast<const uint4*>(ksp + d0);
+            s_words[wi] = *reinterpret_cast<const uint4*>(ksp + d0);
             if (vec) {
-                *reinterpret_cast<uint4*>(qraw) = *reinterpret_cast<const uint4*>(qp + d0);
+                q_words[wi] = *reinterpret_cast<const uint4*>(qp + d0);
             } else {
+                __half tmp[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) qraw[i] = qp[d0 + i];
-            }
-            __half qv[8], qw[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float v = row_ok ? __half2float(qraw[i]) * __half2float(sraw[i]) : 0.f;   // exact in fp32
-                float hi = __half2float(__float2half_rn(v));
-                float lo = __half2float(__float2half_rn(v - hi));
-                if (PAIR) { hi = (g & 1) ? lo : hi; lo = 0.f; }
-                // odd nibbles enter the A operand multiplied by 16
-                qv[i] = __float2half_rn((i & 1) ? hi * 0.0625f : hi);
-                qw[i] = __float2half_rn((i & 1) ? lo * 0.0625f : lo);
-                qsum += ((i & 1) ? 16.f : 1.f) * (__half2float(qv[i]) + __half2float(qw[i]));
-            }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                qb[wi][h][0] = h2_as_u32(__halves2half2(qv[2 * h], qv[2 * h + 4]));
-                qb[wi][h][1] = h2_as_u32(__halves2half2(qv[2 * h + 1], qv[2 * h + 5]));
-                if (!PAIR) {
-                    ql[wi][h][0] = h2_as_u32(__halves2half2(qw[2 * h], qw[2 * h + 4]));
-                    ql[wi][h][1] = h2_as_u32(__halves2half2(qw[2 * h + 1], qw[2 * h + 5]));
-                }
+                for (int i = 0; i < 8; ++i) tmp[i] = qp[d0 + i];
+                q_words[wi] = *reinterpret_cast<const uint4*>(tmp);
             }
         }
     }
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);                 // sum over all D for column g
-    const float c1 = 16777216.f * p.sl2;
-    // rows of this lane: PAIR: row t (columns 2t, 2t+1 are its two parts); else rows 2t and 2t+1
-    const int rw[2] = {PAIR ? t : 2 * t, PAIR ? t : 2 * t + 1};
-    float cq[NR];
-    int lim[NR];
-    {
-        const float qa = __shfl_sync(0xffffffffu, qsum, (2 * t) * 4), qc = __shfl_sync(0xffffffffu, qsum, (2 * t + 1) * 4);
-        if (PAIR) {
-            cq[0] = 8.f * p.sl2 * (qa + qc);
-        } else {
-            cq[0] = 8.f * p.sl2 * qa;
-            cq[NR - 1] = 8.f * p.sl2 * qc;
-        }
-#pragma unroll
-        for (int r = 0; r < NR; ++r) lim[r] = rw[r] < rows_valid ? min(len + rw[r] / rep, capacity) : 0;
-    }
-    // a padded (invalid) row is masked everywhere
-    const int lim_min = rows_valid == (PAIR ? 4 : 8) ? min(len, capacity) : 0;
-
-    float o[NO][4];
-#pragma unroll
-    for (int j = 0; j < NO; ++j)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) o[j][c] = 0.f;
-    float mx[NR], l[NR], lp[NG][NR];
-#pragma unroll
-    for (int r = 0; r < NR; ++r) {
-        mx[r] = -INFINITY;
-        l[r] = 0.f;
-#pragma unroll
-        for (int q = 0; q < NG; ++q) lp[q][r] = 0.f;
-    }
-
     unsigned char* ring = fsm + warp * L::WARP_BYTES;
     const int64_t head_words = int64_t(p.hkv) * NW;
     uint32_t live_bits = 0;
@@ -1022,6 +968,76 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
     for (int i = 0; i < kFastStages - 1; ++i) {
         if (i < n_my) issue(i, i, sc_ring[i]);
         cp_async_commit();
+    }
+
+    // ---- Q'^T fragments (B operand), column n = g; lane t covers words 4t..4t+3.
+    // Q' = q * ks is exact in fp32 and is carried as a high and a low fp16 part: rounded to one fp16 it
+    // would shift every score of the row by the same channel-wise error, which does not average out over
+    // the tokens.
+    uint32_t qb[KWT][2][2], ql[PAIR ? 1 : KWT][2][2];
+    float qsum = 0.f;
+    {
+#pragma unroll
+        for (int wi = 0; wi < KWT; ++wi) {
+            __half qraw[8], sraw[8];
+            *reinterpret_cast<uint4*>(sraw) = s_words[wi];
+            *reinterpret_cast<uint4*>(qraw) = q_words[wi];
+            __half qv[8], qw[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float v = row_ok ? __half2float(qraw[i]) * __half2float(sraw[i]) : 0.f;   // exact in fp32
+                float hi = __half2float(__float2half_rn(v));
+                float lo = __half2float(__float2half_rn(v - hi));
+                if (PAIR) { hi = (g & 1) ? lo : hi; lo = 0.f; }
+                // odd nibbles enter the A operand multiplied by 16
+                qv[i] = __float2half_rn((i & 1) ? hi * 0.0625f : hi);
+                qw[i] = __float2half_rn((i & 1) ? lo * 0.0625f : lo);
+                qsum += ((i & 1) ? 16.f : 1.f) * (__half2float(qv[i]) + __half2float(qw[i]));
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                qb[wi][h][0] = h2_as_u32(__halves2half2(qv[2 * h], qv[2 * h + 4]));
+                qb[wi][h][1] = h2_as_u32(__halves2half2(qv[2 * h + 1], qv[2 * h + 5]));
+                if (!PAIR) {
+                    ql[wi][h][0] = h2_as_u32(__halves2half2(qw[2 * h], qw[2 * h + 4]));
+                    ql[wi][h][1] = h2_as_u32(__halves2half2(qw[2 * h + 1], qw[2 * h + 5]));
+                }
+            }
+        }
+    }
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);                 // sum over all D for column g
+    const float c1 = 16777216.f * p.sl2;
+    // rows of this lane: PAIR: row t (columns 2t, 2t+1 are its two parts); else rows 2t and 2t+1
+    const int rw[2] = {PAIR ? t : 2 * t, PAIR ? t : 2 * t + 1};
+    float cq[NR];
+    int lim[NR];
+    {
+        const float qa = __shfl_sync(0xffffffffu, qsum, (2 * t) * 4), qc = __shfl_sync(0xffffffffu, qsum, (2 * t + 1) * 4);
+        if (PAIR) {
+            cq[0] = 8.f * p.sl2 * (qa + qc);
+        } else {
+            cq[0] = 8.f * p.sl2 * qa;
+            cq[NR - 1] = 8.f * p.sl2 * qc;
+        }
+#pragma unroll
+        for (int r = 0; r < NR; ++r) lim[r] = rw[r] < rows_valid ? min(len + rw[r] / rep, capacity) : 0;
+    }
+    // a padded (invalid) row is masked everywhere
+    const int lim_min = rows_valid == (PAIR ? 4 : 8) ? min(len, capacity) : 0;
+
+    float o[NO][4];
+#pragma unroll
+    for (int j = 0; j < NO; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[j][c] = 0.f;
+    float mx[NR], l[NR], lp[NG][NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        mx[r] = -INFINITY;
+        l[r] = 0.f;
+#pragma unroll
+        for (int q = 0; q < NG; ++q) lp[q][r] = 0.f;
     }
 
     // The loop is unrolled over the ring so that the stage slot, its shared-memory address and

@@ -128,6 +128,20 @@ def test_greedy_tokens_match_oracle(tmp_path, affine, eager, chunk):
         assert runner.graph_replays == 63
 
 
+def test_long_prompt_in_two_large_chunks(tmp_path):
+    """A 450-token prompt in chunks of 290: the first chunk (no prefix, more than 256 rows) goes
+    through torch's fused attention, the second reads its 290-token prefix as int4 and its own
+    160 rows through the chunk kernel in five 32-key tiles per row."""
+    from linkq2_b200.runtime.model.qwen3 import ModelConfig
+    weights = write_checkpoint(tmp_path / "w4")
+    runner = make_runner(tmp_path / "w4", eager=True)
+    g = torch.Generator().manual_seed(12)
+    prompt = torch.randint(0, 127, (450,), generator=g).tolist()
+    (tokens,), _ = generate(runner, [prompt], 24, 290)
+    oracle = oq.OracleQwen3(ModelConfig.from_dict(CFG), weights, kscale=torch.full((2, 1, 64), 0.3), max_tokens=512)
+    assert tokens == oracle.greedy(prompt, 24, chunk=290)
+
+
 def test_temperature_rows_are_sampled_and_greedy_rows_are_not(tmp_path):
     """Per-row temperatures as in the reference's sampler (``execute/sampler.py:8-13``): a row
     at temperature 0 keeps the arg-max, a hot row is drawn from the softmax; the same seed

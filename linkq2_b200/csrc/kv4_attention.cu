@@ -5,24 +5,28 @@
 // (qslab/kernels/kv4/paged_attention.py:11-150: decode kernel, split merge and
 // launcher; qslab/kernels/kv4/grouped_attention.py:7-63: grouped verify).
 //
-// Work decomposition.  One CTA serves one (sequence, KV head, split): all query
-// heads of the GQA group — and for verify all M positions — share a single read
-// of the packed K/V bytes.  Query rows are ordered row = m * rep + head_in_group
-// and cut into tiles of 16; warp w works on row tile w % RT and, when RT < 4, on
-// every (4/RT)-th 16-token block of the split.  Both products run on the
-// warp-level tensor-core op m16n8k16 with fp32 accumulation:
-//   S = Q' K^T : Q' = fp16(q * ks) carries the static per-channel K scale, so K
-//                enters as the exact integers (nibble - 8);
-//   O += P V   : V is dequantised to fp16 (nibble - 8) * vs rounded once, as the
-//                reference's verify kernel does (grouped_attention.py:50-53).
-// Nibbles are unpacked in registers in an order that needs one shift per word;
-// the matching permutation of head channels is applied to Q' once at load and to
-// O once at the write-out.  Scores, the running maximum, the denominator and O
-// stay fp32.
+// Three kernels share the launcher at the end of this file:
+//   kv4_decode_fast_kernel  at most 8 query rows per KV head (decode, D 64 or 128): per-warp cp.async
+//                           rings, the cache as the 16-row MMA operand, codes as fp16 subnormals;
+//   kv4_verify_kernel       17..64 query rows per KV head at D = 128 (16-position verify, and the
+//                           prefix part of chunked prefill): the tile dequantised once per CTA into
+//                           shared memory, ldmatrix operands;
+//   kv4_attention_kernel    every other geometry: one CTA per (sequence, KV head, split), query rows
+//                           row = m * rep + head_in_group cut into tiles of 16, warp w on row tile
+//                           w % RT and on every (4/RT)-th 16-token block, operands unpacked in registers.
+// In all of them every query head of a GQA group - and for verify all M positions - shares a single
+// read of the packed K/V bytes, both products run on the warp-level tensor-core op m16n8k16 with fp32
+// accumulation, and scores, running maximum, denominator and O stay fp32:
+//   S = Q' K^T : Q' = q * ks carries the static per-channel K scale, so K enters as exact integers;
+//                Q' is exact in fp32 and is split into a high and a low fp16 part (one rounded fp16
+//                would shift all scores of a row by the same channel-wise error);
+//   O += P' V  : P' = p * vs carries the V scale of the token and group, V enters as exact integers
+//                (the generic kernel dequantises V to fp16 (nibble - 8) * vs instead, as the
+//                reference's verify kernel does, grouped_attention.py:50-53).
 //
 // Splits.  The split count depends on shapes only.  Each CTA writes an fp32
 // partial (O, max, denominator) per row, takes a ticket, and the last CTA of a
-// (sequence, KV head) merges the partials in split order and writes fp16.
+// (sequence, KV head) merges the partials in split order (merge_splits) and writes fp16.
 #include <math.h>
 
 #include <mutex>
@@ -810,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, 3) kv4_verify_kernel(const AttnParam
 //   O^T[dim, row]  += V^T[dim, token] . P'[token, row]   A = V nibbles, B = P'^T
 // Nibbles enter A as fp16 subnormals by masking alone (u * 2^-24, or 16u * 2^-24 for odd
 // nibbles); the offsets and scales are applied outside the MMAs:
-//   S  = 2^24 * acc - 8 * sum_d Q'[row, d]          (Q' = fp16(q * ks), /16 on odd slots)
+//   S  = 2^24 * acc - 8 * sum_d Q'[row, d]          (Q' = q * ks in two fp16 parts, /16 on odd slots)
 //   O  = 2^24 * acc - 8 * sum_t P'[t, row],  P'[t, row] = p[t, row] * vs[t, group]
 // P' is moved from the accumulator layout to the B layout with movmatrix.
 // =====================================================================================

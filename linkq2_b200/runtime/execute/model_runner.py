@@ -346,9 +346,14 @@ class ModelRunner:
         for them (``last_logits``).  Rows with a temperature above 1e-6 are drawn from
         softmax(logits / temperature) by the exponential race of
         ``qslab/runtime/execute/sampler.py:8-13``: arg-max of probs / Exp(1) noise."""
-        temps = torch.as_tensor(self.temperature, dtype=torch.float32, device=hidden.device)
-        if bool((temps > 1e-6).any()):
+        temperature = self.temperature
+        if isinstance(temperature, (int, float)):
+            hot = temperature > 1e-6                          # decided on the host: no device round trip per step
+        else:
+            hot = bool((torch.as_tensor(temperature) > 1e-6).any())
+        if hot:
             self.last_logits = self.model.compute_logits(hidden)
+            temps = torch.as_tensor(temperature, dtype=torch.float32, device=hidden.device)
             temps = temps.expand(hidden.shape[0]) if temps.dim() == 0 else temps
             greedy = self.last_logits.argmax(dim=-1)
             probs = torch.softmax(self.last_logits.float() / temps.clamp_min(1e-6).unsqueeze(1), dim=-1)

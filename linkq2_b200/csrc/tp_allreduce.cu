@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const __half* 
 }
 
 // ---------------------------------------------------------------- all-reduce + residual RMSNorm
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 256;     // thread count and chunk order of rmsnorm_kernel: the two must round alike
 constexpr int kNormMaxChunks = 4;     // 8 halves per chunk per thread: hidden <= 8192
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -170,6 +170,11 @@ __device__ __forceinline__ float warp_sum(float v) {
 // h = fp16(sum over ranks of x_r) (rank order, fp32), then exactly the residual RMSNorm of
 // qslab/runtime/model/primitives.py:23-30 on h: s = fp32(h) + fp32(residual),
 // residual_out = fp16(s), out = fp16(s * rsqrt(mean(s^2) + eps)) * weight.
+// CH: chunks per thread this instantiation provides for (hidden <= 2048 * CH); W: ranks it provides for.
+// Both bound the registers that hold peers' words in flight: the kernel shares its SM with the CTAs of the
+// next projection, which programmatic dependent launch brings in early, so a fat CTA here delays them
+// (218 registers per thread cost 7 % of a two-GPU decode step).
+template <int CH, int W>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
     const __half* x, int64_t x_stride, const __half* residual, const __half* __restrict__ weight, __half* out,
     __half* residual_out, const int hidden, const float eps, const PeerTable peers, const int rank,
@@ -189,9 +194,9 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
     const int chunks = hidden / 8;
 
     // my addend, and its flagged copy into every peer
-    uint4 own[kNormMaxChunks];
+    uint4 own[CH];
 #pragma unroll
-    for (int c = 0; c < kNormMaxChunks; ++c) {
+    for (int c = 0; c < CH; ++c) {
         const int idx = tid + c * kNormThreads;
         if (idx < chunks) {
             own[c] = *reinterpret_cast<const uint4*>(x + int64_t(row) * x_stride + idx * 8);
@@ -205,34 +210,72 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
             }
         }
     }
-    // gather, sum in rank order, residual add
-    float v[kNormMaxChunks][8];
+    // gather, sum in rank order, residual add.  All peers' words of all of this thread's chunks are requested
+    // before the first one is examined: looked at one after the other, the round trips of a thread add up
+    // (14 in a row at eight ranks with two chunks per thread), which is what an exchange used to cost there.
+    float v[CH][8];
     float ss = 0.f;
     bool gave_up = false;
     long long budget = poll_limit;                      // polls left to this thread, over all its waits
-#pragma unroll
-    for (int c = 0; c < kNormMaxChunks; ++c) {
+    // Words in flight per thread: at most eight peer entries (64 registers), taken as whole chunks when the
+    // ranks are few and as groups of four peers of one chunk when they are many.
+    constexpr int G = W < 4 ? W : 4;                     // peers requested together
+    constexpr int AHEAD = CH * W <= 8 ? CH : (2 * W <= 8 && CH >= 2 ? 2 : 1);   // chunks requested together
+    uint4 lo[AHEAD][G], hi[AHEAD][G];
+    auto request = [&](int c, int slot, int p0) {
         const int idx = tid + c * kNormThreads;
-        if (idx < chunks) {
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (int p = 0; p < world; ++p) {
-                if (p == rank) {
-                    add8(acc, own[c]);
-                    continue;
-                }
-                const unsigned char* src = mine + ll + size_t(p) * 2 * max_bytes + (size_t(row) * chunks + idx) * 32;
-                uint4 lo, hi;
-                for (;;) {
-                    lo = ld_volatile_u4(src);
-                    hi = ld_volatile_u4(src + 16);
-                    if (lo.y == seq && lo.w == seq && hi.y == seq && hi.w == seq) break;
-                    if (--budget <= 0) {                // spent: this and every later wait ends after one look
-                        gave_up = true;
-                        break;
-                    }
-                }
-                add8(acc, make_uint4(lo.x, lo.z, hi.x, hi.z));
+        if (idx >= chunks) return;
+        const unsigned char* base = mine + ll + (size_t(row) * chunks + idx) * 32;
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+            const int p = p0 + j;
+            if (p < world && p != rank) {
+                lo[slot][j] = ld_volatile_u4(base + size_t(p) * 2 * max_bytes);
+                hi[slot][j] = ld_volatile_u4(base + size_t(p) * 2 * max_bytes + 16);
             }
+        }
+    };
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int idx = tid + c * kNormThreads;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int p0 = 0; p0 < W; p0 += G) {
+            if (W <= G) {                                // all peers fit: the next AHEAD chunks at once
+                if (c % AHEAD == 0) {
+#pragma unroll
+                    for (int a = 0; a < AHEAD; ++a)
+                        if (c + a < CH) request(c + a, a, 0);
+                }
+            } else {
+                request(c, 0, p0);
+            }
+            if (idx < chunks) {
+                const int slot = W <= G ? c % AHEAD : 0;
+                const unsigned char* base = mine + ll + (size_t(row) * chunks + idx) * 32;
+#pragma unroll
+                for (int j = 0; j < G; ++j) {
+                    const int p = p0 + j;
+                    if (p >= world) continue;
+                    if (p == rank) {
+                        add8(acc, own[c]);
+                        continue;
+                    }
+                    const unsigned char* src = base + size_t(p) * 2 * max_bytes;
+                    uint4 a = lo[slot][j], b = hi[slot][j];
+                    while (!(a.y == seq && a.w == seq && b.y == seq && b.w == seq)) {
+                        if (--budget <= 0) {            // spent: this and every later wait ends after one look
+                            gave_up = true;
+                            break;
+                        }
+                        a = ld_volatile_u4(src);
+                        b = ld_volatile_u4(src + 16);
+                    }
+                    add8(acc, make_uint4(a.x, a.z, b.x, b.z));
+                }
+            }
+        }
+        if (idx < chunks) {
             const uint4 rr = *reinterpret_cast<const uint4*>(residual + int64_t(row) * hidden + idx * 8);
             const __half2* r = reinterpret_cast<const __half2*>(&rr);
             __half2 o[4];
@@ -257,7 +300,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
     for (int w = 0; w < kNormThreads / 32; ++w) total += partial[w];
     const float rs = rsqrtf(total / float(hidden) + eps);
 #pragma unroll
-    for (int c = 0; c < kNormMaxChunks; ++c) {
+    for (int c = 0; c < CH; ++c) {
         const int idx = tid + c * kNormThreads;
         if (idx < chunks) {
             const uint4 wr = *reinterpret_cast<const uint4*>(weight + idx * 8);
@@ -385,11 +428,17 @@ static int rmsnorm_allreduce_impl(const void* x, int64_t x_row_stride, const voi
         peers.base[p] = p < world ? static_cast<unsigned char*>(buffers[p]) : nullptr;
         if (p < world && !peers.base[p]) return LQ2_ERR_ARG;
     }
-    return launch_pdl(rmsnorm_allreduce_kernel, dim3(rows), dim3(kNormThreads), 0, static_cast<cudaStream_t>(stream), 1,
-                      static_cast<const __half*>(x), x_row_stride, static_cast<const __half*>(residual),
-                      static_cast<const __half*>(weight), static_cast<__half*>(out),
-                      static_cast<__half*>(residual_out), hidden, eps, peers, rank, world, max_message_bytes, pushed,
-                      g_poll_limit.load(std::memory_order_relaxed));
+    auto launch = [&](auto kernel) {
+        return launch_pdl(kernel, dim3(rows), dim3(kNormThreads), 0, static_cast<cudaStream_t>(stream), 1,
+                          static_cast<const __half*>(x), x_row_stride, static_cast<const __half*>(residual),
+                          static_cast<const __half*>(weight), static_cast<__half*>(out),
+                          static_cast<__half*>(residual_out), hidden, eps, peers, rank, world, max_message_bytes,
+                          pushed, g_poll_limit.load(std::memory_order_relaxed));
+    };
+    const int ch = hidden <= 8 * kNormThreads ? 1 : (hidden <= 16 * kNormThreads ? 2 : 4);
+    if (world <= 2) return ch == 1 ? launch(rmsnorm_allreduce_kernel<1, 2>) : ch == 2 ? launch(rmsnorm_allreduce_kernel<2, 2>) : launch(rmsnorm_allreduce_kernel<4, 2>);
+    if (world <= 4) return ch == 1 ? launch(rmsnorm_allreduce_kernel<1, 4>) : ch == 2 ? launch(rmsnorm_allreduce_kernel<2, 4>) : launch(rmsnorm_allreduce_kernel<4, 4>);
+    return ch == 1 ? launch(rmsnorm_allreduce_kernel<1, 8>) : ch == 2 ? launch(rmsnorm_allreduce_kernel<2, 8>) : launch(rmsnorm_allreduce_kernel<4, 8>);
 }
 
 int lq2_rmsnorm_allreduce(const void* x, int64_t x_row_stride, const void* residual, const void* weight, void* out,

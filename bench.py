@@ -467,7 +467,7 @@ def run_b200(args):
             bucket = graphs.stage_packed(packed_all[i], batch, width)
             graphs.run_graph(1, bucket)
             hidden = graphs.families[1].buffers['outputs'][:batch]
-            ids = model.compute_logits(hidden).argmax(dim=-1)
+            ids = model.greedy_tokens(hidden)          # arg-max; a (value, index) exchange under tensor parallelism
             history[i] = ids
         ev1.record()
     barrier()

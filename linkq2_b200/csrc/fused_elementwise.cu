@@ -41,6 +41,13 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
     const int chunks = hidden / 8;
     float v[kNormMaxChunks][8];
     float ss = 0.f;
+    // the norm weights are requested with the inputs, not after the reduction: one memory round trip less
+    uint4 norm_w[kNormMaxChunks];
+#pragma unroll
+    for (int c = 0; c < kNormMaxChunks; ++c) {
+        const int idx = tid + c * kNormThreads;
+        if (idx < chunks) norm_w[c] = *reinterpret_cast<const uint4*>(weight + idx * 8);
+    }
 #pragma unroll
     for (int c = 0; c < kNormMaxChunks; ++c) {
         const int idx = tid + c * kNormThreads;
@@ -81,8 +88,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
     for (int c = 0; c < kNormMaxChunks; ++c) {
         const int idx = tid + c * kNormThreads;
         if (idx < chunks) {
-            const uint4 wr = *reinterpret_cast<const uint4*>(weight + idx * 8);
-            const __half2* w = reinterpret_cast<const __half2*>(&wr);
+            const __half2* w = reinterpret_cast<const __half2*>(&norm_w[c]);
             __half2 o[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)

@@ -53,6 +53,11 @@ constexpr long long kDefaultPollLimit = 1ll << 22;      // a few seconds of poll
 
 __device__ unsigned int g_lq2_allreduce_timeouts = 0;
 
+__device__ __forceinline__ unsigned int ld_volatile_u32(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.volatile.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ uint4 ld_volatile_u4(const void* p) {
     uint4 v;
     asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];\n"
@@ -182,24 +187,33 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
     pdl_launch_dependents();
     pdl_wait();
     __shared__ float partial[kNormThreads / 32];
-    __shared__ unsigned int s_seq;
     const int row = blockIdx.x, tid = threadIdx.x;
     unsigned char* mine = peer_base(peers, rank);
     unsigned int* calls = reinterpret_cast<unsigned int*>(mine);
     unsigned int* done = calls + 1;
-    if (tid == 0) s_seq = *calls + 1;
-    __syncthreads();
-    const unsigned int seq = s_seq;
-    const size_t ll = llslots_offset(world, max_bytes) + size_t(seq & 1u) * world * 2 * max_bytes;
     const int chunks = hidden / 8;
-
-    // my addend, and its flagged copy into every peer
-    uint4 own[CH];
+    // Everything that does not depend on the call's sequence number is requested at once - the number itself
+    // (every thread reads it: the last CTA of a call advances it only after all CTAs have arrived at the end),
+    // this rank's addend, the residual and the norm weight - so that the kernel is two memory round trips
+    // (these, then the peers' words) instead of one per operand.
+    const unsigned int seq = ld_volatile_u32(calls) + 1;
+    uint4 own[CH], res_w[CH], norm_w[CH];
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
         const int idx = tid + c * kNormThreads;
         if (idx < chunks) {
             own[c] = *reinterpret_cast<const uint4*>(x + int64_t(row) * x_stride + idx * 8);
+            res_w[c] = *reinterpret_cast<const uint4*>(residual + int64_t(row) * hidden + idx * 8);
+            norm_w[c] = *reinterpret_cast<const uint4*>(weight + idx * 8);
+        }
+    }
+    const size_t ll = llslots_offset(world, max_bytes) + size_t(seq & 1u) * world * 2 * max_bytes;
+
+    // the flagged copy of my addend into every peer
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int idx = tid + c * kNormThreads;
+        if (idx < chunks) {
             const uint4 lo = make_uint4(own[c].x, seq, own[c].y, seq), hi = make_uint4(own[c].z, seq, own[c].w, seq);
             const size_t off = ll + size_t(rank) * 2 * max_bytes + (size_t(row) * chunks + idx) * 32;
             for (int p = 0; p < world; ++p) {
@@ -276,8 +290,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
             }
         }
         if (idx < chunks) {
-            const uint4 rr = *reinterpret_cast<const uint4*>(residual + int64_t(row) * hidden + idx * 8);
-            const __half2* r = reinterpret_cast<const __half2*>(&rr);
+            const __half2* r = reinterpret_cast<const __half2*>(&res_w[c]);
             __half2 o[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -303,8 +316,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_allreduce_kernel(
     for (int c = 0; c < CH; ++c) {
         const int idx = tid + c * kNormThreads;
         if (idx < chunks) {
-            const uint4 wr = *reinterpret_cast<const uint4*>(weight + idx * 8);
-            const __half2* w = reinterpret_cast<const __half2*>(&wr);
+            const __half2* w = reinterpret_cast<const __half2*>(&norm_w[c]);
             __half2 o[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)

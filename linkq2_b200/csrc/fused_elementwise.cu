@@ -161,23 +161,42 @@ __global__ void __launch_bounds__(128) pre_attention_kernel(const PreAttnParams 
     const __half* wgt = is_q ? p.q_weight : p.k_weight;
     const int d0 = EPL * lane;
 
+    // Everything whose address is known now is requested now - the position (the rotation table row
+    // depends on it), the pool slot and the value row of a key head, the norm weights - so that the
+    // kernel is two memory round trips, not one per operand.
+    const int64_t position = p.positions[token];
+    const bool kv_head = !is_q && p.slots != nullptr;
+    const int64_t slot = kv_head ? int64_t(p.slots[token]) : -1;
     float a[EPL], b[EPL];                    // first half, second half
-    float ss = 0.f;
+    float va[EPL], vb[EPL];
+    __half wa[EPL], wb[EPL];
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
         a[i] = __half2float(src[d0 + i]);
         b[i] = __half2float(src[HALF + d0 + i]);
-        ss += a[i] * a[i] + b[i] * b[i];
+        wa[i] = wgt[d0 + i];
+        wb[i] = wgt[HALF + d0 + i];
     }
+    if (kv_head) {
+        const __half* vsrc = p.v + int64_t(token) * p.v_stride + h * D;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            va[i] = __half2float(vsrc[d0 + i]);
+            vb[i] = __half2float(vsrc[HALF + d0 + i]);
+        }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) ss += a[i] * a[i] + b[i] * b[i];
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / float(D) + p.eps);
-    const float* cs = p.cos_sin + p.positions[token] * D;
+    const float* cs = p.cos_sin + position * D;
     __half oa[EPL], ob[EPL];
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
         // norm -> fp16, * weight in fp16, rotation in fp32 -> fp16
-        const float x1 = __half2float(__hmul(__float2half_rn(a[i] * r), wgt[d0 + i]));
-        const float x2 = __half2float(__hmul(__float2half_rn(b[i] * r), wgt[HALF + d0 + i]));
+        const float x1 = __half2float(__hmul(__float2half_rn(a[i] * r), wa[i]));
+        const float x2 = __half2float(__hmul(__float2half_rn(b[i] * r), wb[i]));
         const float c = cs[d0 + i], s = cs[HALF + d0 + i];
         oa[i] = __float2half_rn(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
         ob[i] = __float2half_rn(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
@@ -209,15 +228,10 @@ __global__ void __launch_bounds__(128) pre_attention_kernel(const PreAttnParams 
         }
     }
     if (!p.slots) return;
-    const int64_t slot = p.slots[token];
     const bool write = slot >= 0 && slot < p.num_slots;
-    const __half* vsrc = p.v + int64_t(token) * p.v_stride + h * D;
-    float va[EPL], vb[EPL];
     float m1 = 0.f, m2 = 0.f;
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
-        va[i] = __half2float(vsrc[d0 + i]);
-        vb[i] = __half2float(vsrc[HALF + d0 + i]);
         m1 = fmaxf(m1, fabsf(va[i]));
         m2 = fmaxf(m2, fabsf(vb[i]));
     }

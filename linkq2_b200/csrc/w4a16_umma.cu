@@ -61,6 +61,7 @@ struct UParams {
     int early_weights;    // request weight bytes before the previous kernel of the stream has finished
     int silu;             // columns are interleaved [4 gate | 4 up]: write silu(gate) * up, N / 2 wide
     PushTarget push;      // tensor-parallel peers that receive the output as flagged words (world 0: none)
+    const unsigned int* exchange_calls;   // this rank's exchange call counter (null without peers)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -240,6 +241,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     constexpr int RS = L::R_STAGES, AS = L::A_STAGES, UK = L::UK, ISS = L::ISS;
     const uint32_t bars = smem_u32(smem + L::DATA_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::DATA_BYTES + L::NBARS * 8);
+    volatile unsigned int* push_seq = tmem_slot + 2;          // the 16 bytes behind the barriers hold both
     auto raw_full = [&](int s) { return bars + 8 * s; };               // TMA bytes of raw stage s landed
     auto raw_free = [&](int s) { return bars + 8 * (RS + s); };        // MMAs that read its activations are done
     // k-half h of A tile s written by the dequant warps that own it (all of them when there is one issuer)
@@ -360,6 +362,10 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
     } else if (warp < 2 + kDequantThreads / 32) {
         // ------------------------------------------------------------ dequantise
         pdl_wait();
+        // The exchange's call counter is read here, long before the epilogue needs it, so that its memory
+        // round trip is off the end of the kernel; the kernels that advance it precede this one in the stream.
+        if (p.exchange_calls && tid == 64)
+            *push_seq = *reinterpret_cast<const volatile unsigned int*>(p.exchange_calls) + 1;   // calls completed + 1
         // A warp reaches the 32 TMEM lanes of its quarter (warp % 4); lane = output channel.  Two
         // warps share a quarter and take k8 rows 0-3 and 4-7 of the stage.
         const int quarter = warp & 3, khalf = (warp - 2) >> 2;
@@ -504,11 +510,7 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
             unsigned int seq = 0;
             size_t ll = 0;
             if (world > 1) {
-                const unsigned char* mine = nullptr;
-#pragma unroll
-                for (int peer = 0; peer < kMaxWorld; ++peer)
-                    if (peer == me) mine = p.push.peers.base[peer];
-                seq = *reinterpret_cast<const unsigned int*>(mine) + 1;                  // exchanges completed + 1
+                seq = *push_seq;                       // written before the barrier above
                 ll = llslots_offset(world, p.push.max_bytes) +
                      (size_t(seq & 1u) * world + me) * 2 * p.push.max_bytes;
             }
@@ -710,9 +712,11 @@ int w4a16_umma_launch(const __half* x, int64_t ldx, const int32_t* packed, const
     p.early_weights = early_weight_fetch() ? 1 : 0;
     p.silu = silu;
     p.push = PushTarget{};
+    p.exchange_calls = nullptr;
     if (push) {
         if (pl.mb > 64 || silu) return LQ2_ERR_SHAPE;      // only the pushed-reduction epilogue carries it
         p.push = *push;
+        p.exchange_calls = reinterpret_cast<const unsigned int*>(push->peers.base[push->rank]);
     }
     switch (pl.mb) {
         case 16: return launch_umma_z<16>(x, ldx, packed, scales, zeros, p, pl, st);

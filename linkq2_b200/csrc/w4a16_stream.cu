@@ -98,6 +98,9 @@ __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity) {
         if (mbar_try_wait(bar, parity)) return;
     atomicAdd(&g_lq2_w4_wait_timeouts, 1u);
 }
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(map) : "memory");
+}
 // 2-D tiled TMA load (one CTA is the only receiver): box at element coordinates (c0 = innermost, c1) -> shared memory
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
     asm volatile(
@@ -158,6 +161,12 @@ __global__ void __launch_bounds__(Layout<NJ, WN, GPS>::THREADS, (NJ <= 2 ? 4 : (
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
+    if (threadIdx.x == 0) {                  // the tensor maps' descriptors are on their way before the first copy needs them
+        prefetch_tensormap(&map_w);
+        prefetch_tensormap(&map_x);
+        prefetch_tensormap(&map_s);
+        prefetch_tensormap(&map_z);
+    }
     const int m0 = blockIdx.z * MT;
     const int rows = min(MT, p.m - m0);
     const int tile_n0 = blockIdx.x * TN;

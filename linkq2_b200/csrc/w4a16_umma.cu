@@ -93,6 +93,9 @@ __device__ __forceinline__ void mbar_wait_bounded(uint32_t bar, uint32_t parity)
         if (mbar_try_wait(bar, parity)) return;
     atomicAdd(&g_lq2_umma_wait_timeouts, 1u);
 }
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(map) : "memory");
+}
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
@@ -251,6 +254,12 @@ w4a16_umma_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_consta
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile_n0 = blockIdx.x * kUM;
+    if (threadIdx.x == 0) {                  // the tensor maps' descriptors are on their way before the first copy needs them
+        prefetch_tensormap(&map_w);
+        prefetch_tensormap(&map_x);
+        prefetch_tensormap(&map_s);
+        prefetch_tensormap(&map_z);
+    }
     const int m0 = blockIdx.z * MB;
     const int rows = min(MB, p.m - m0);
     const int total_stages = (p.k + UK - 1) / UK;

@@ -1158,21 +1158,25 @@ __global__ void __launch_bounds__(kFastThreads, 2) kv4_decode_fast_kernel(const 
                 const uint32_t sA = __shfl_sync(0xffffffffu, sc_cur, 16 * b16 + g);
                 const uint32_t sB = __shfl_sync(0xffffffffu, sc_cur, 16 * b16 + g + 8);
                 const unsigned char* vrow = vb + (16 * b16) * L::VROW;
+                const float2 fA = __half22float2(u32_as_h2(sA)), fB = __half22float2(u32_as_h2(sB));   // both groups' scales
 #pragma unroll
                 for (int q = 0; q < NG; ++q) {
-                    const float fa = __half2float(__ushort_as_half((unsigned short)(q ? (sA >> 16) : (sA & 0xffff))));
-                    const float fb = __half2float(__ushort_as_half((unsigned short)(q ? (sB >> 16) : (sB & 0xffff))));
+                    const float fa = q ? fA.y : fA.x;
+                    const float fb = q ? fB.y : fB.x;
                     // P' = p * vs enters the MMA as fp16: PAIR carries its rounding remainder in the odd column;
                     // otherwise it is one fp16.  The offset term -8 * sum P' must be summed from the same
                     // rounded values, or the rounding noise would enter the result multiplied by 8.
                     uint32_t h01, h23;
                     if (PAIR) {
+                        // both tokens' parts in packed conversions
                         const float xa = pr[0] * fa, xb = pr[1] * fb;
-                        const __half ha = __float2half_rn(xa), hb = __float2half_rn(xb);
-                        const __half la = __float2half_rn(xa - __half2float(ha)), lb = __float2half_rn(xb - __half2float(hb));
-                        h01 = h2_as_u32(__halves2half2(ha, la));
-                        h23 = h2_as_u32(__halves2half2(hb, lb));
-                        lp[q][0] += (__half2float(ha) + __half2float(la)) + (__half2float(hb) + __half2float(lb));
+                        const __half2 hab = __floats2half2_rn(xa, xb);
+                        const float2 hf = __half22float2(hab);
+                        const __half2 lab = __floats2half2_rn(xa - hf.x, xb - hf.y);
+                        h01 = __byte_perm(h2_as_u32(hab), h2_as_u32(lab), 0x5410);       // (high, low) of token A
+                        h23 = __byte_perm(h2_as_u32(hab), h2_as_u32(lab), 0x7632);       // of token B
+                        const float2 lf = __half22float2(lab);
+                        lp[q][0] += (hf.x + lf.x) + (hf.y + lf.y);
                     } else {
                         h01 = pack_h2(pr[0] * fa, pr[NR - 1] * fa);
                         h23 = pack_h2(pr[NR] * fb, pr[2 * NR - 1] * fb);

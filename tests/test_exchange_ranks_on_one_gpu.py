@@ -73,10 +73,12 @@ def test_pushed_exchange_of_emulated_ranks(world, rows, k, hidden):
             lib.lq2_allreduce_buffer_close(b, 1)
 
 
+@pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("world", [4, 8])
-def test_sending_exchange_reaches_the_rank_launched_last(world):
-    """The sending variant (``lq2_rmsnorm_allreduce``: every rank stores its own rows into all
-    buffers, then gathers) with the emulated ranks launched one after the other.  Only the rank
+def test_sending_exchange_reaches_the_rank_launched_last(world, fused):
+    """The sending variants (``lq2_rmsnorm_allreduce`` and the plain ``lq2_allreduce_fp16``: every
+    rank stores its own rows into all buffers, then gathers) with the emulated ranks launched
+    one after the other.  Only the rank
     launched last can find all its peers' rows, so only its result is checked; the earlier ones
     run against a budget of a few thousand polls, give up and are counted - the bounded wait
     at work, nothing hangs.  The last rank rotates, so every rank is the receiver once."""
@@ -98,14 +100,21 @@ def test_sending_exchange_reaches_the_rank_launched_last(world):
             want_out, want_res = rmsnorm(acc.half(), w, 1e-6, res)
             order = [r for r in range(world) if r != last] + [last]
             before = exchanges[0].timeouts()
+            def run(r):
+                if fused:
+                    return rmsnorm_allreduce(xs[r], w, 1e-6, res, exchanges[r])
+                return exchanges[r].all_reduce(xs[r].clone())
             for r in order[:-1]:
-                rmsnorm_allreduce(xs[r], w, 1e-6, res, exchanges[r])
+                run(r)
             gave_up = exchanges[0].timeouts()
             assert gave_up > before
-            got_out, got_res = rmsnorm_allreduce(xs[last], w, 1e-6, res, exchanges[last])
+            got = run(last)
             torch.cuda.synchronize()
             assert exchanges[0].timeouts() == gave_up, "the rank launched last found everything it waited for"
-            assert torch.equal(got_res, want_res) and torch.equal(got_out, want_out), last
+            if fused:
+                assert torch.equal(got[1], want_res) and torch.equal(got[0], want_out), last
+            else:
+                assert torch.equal(got, acc.half()), last
     finally:
         exchanges[0].set_poll_limit(previous)
         for b in bufs:
